@@ -1,0 +1,699 @@
+// qmatvec.cu -- streaming GGUF-block matvec on CUDA cores (batch 1) for sm_100a,
+// plus the exact dequantizer and a generic per-row kernel for odd shapes.
+//
+// Streaming kernel (qmv_stream_kernel):
+//   * Work is a grid of cells: (row group of kRows rows) x (unit of 256 weights
+//     = one K-quant super-block or eight 32-weight blocks). Every warp of the
+//     persistent grid owns a contiguous, equal-sized range of cells in
+//     row-group-major order, so HBM traffic is balanced to +-1 cell per warp
+//     whatever n_out and k are.
+//   * A warp step covers up to 8 consecutive units of one row group. Lane 0
+//     copies the step's kRows row segments (contiguous bytes of W) into a
+//     private ring of shared-memory stages with cp.async.bulk; the ring runs
+//     up to kMaxStages steps ahead of the decode, so the copy engine keeps
+//     ~100 KB per SM in flight.
+//   * x is staged once per CTA in shared memory, permuted per type so that
+//     lane (unit j, quarter c) reads its 64 activations with 16 conflict-free
+//     128-bit loads, then keeps them in registers for all kRows rows.
+//   * Four lanes share a unit; lane c decodes a quarter (64 weights): the
+//     quant bits are moved into the top of an fp32 mantissa with one PRMT per
+//     weight (f = 0.5 + q * 2^-(bits+1), exact) and accumulated with packed
+//     fma.rn.f32x2, so sum_k q*x = 2^(bits+1)*S - 2^bits*X with X = sum_k x
+//     precomputed per quarter during staging. Scales are applied once per
+//     sub-block.
+//   * Row sums are reduced with warp shuffles. A row group split between
+//     warps is combined deterministically: every warp writes its partial to
+//     the workspace, and the last to arrive (acq_rel counter) adds the
+//     partials in warp order and writes y.
+#include "hesa_common.cuh"
+#include "qtypes.cuh"
+#include "qmatvec.h"
+
+#include <cuda/atomic>
+
+namespace hesa_cuda {
+
+// The library's sticky status word (0 = healthy); kernels get its address.
+__device__ int g_hesa_status = 0;
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRows = 4;           // rows per row group: x register reuse factor
+constexpr int kUnitsPerStep = 8;   // units per warp step (4 lanes per unit)
+constexpr int kXStride = 68;       // floats per (unit, quarter) in smem: 64 + 4 pad
+constexpr int kMaxStages = 4;
+constexpr int kMaxSmem = 227 * 1024;
+
+__host__ __device__ constexpr int unit_bytes(int qt) {
+    return qt == kQ4_K ? 144 : qt == kQ5_K ? 176 : qt == kQ6_K ? 210 : qt == kQ4_0 ? 144 : 272;
+}
+
+__host__ __device__ constexpr int slot_bytes(int qt) {
+    // one row segment of up to kUnitsPerStep units, plus room for the <16 B
+    // alignment offset of its first byte and the 4-byte over-read of the
+    // unaligned loads
+    return ((kUnitsPerStep * unit_bytes(qt) + 15) / 16) * 16 + 32;
+}
+
+__host__ __device__ constexpr int stage_bytes(int qt) { return kRows * slot_bytes(qt); }
+
+// Slot (quarter c, index i) of activation P (0..255 inside a unit), in the
+// order the decoders consume it.
+template <int QT>
+__device__ __forceinline__ void unit_pos_to_slot(int P, int& c, int& i) {
+    if constexpr (QT == kQ6_K) {
+        const int h = P >> 7, g = (P >> 5) & 3, s2 = (P >> 4) & 1, t = P & 15;
+        c = 2 * h + s2;
+        i = 16 * g + t;
+    } else {
+        c = P >> 6;
+        i = P & 63;
+    }
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// 16 bytes from a 2-byte aligned shared address: five aligned words, realigned
+// with PRMT (selector 0x5432 takes bytes 2..5 of the pair).
+__device__ __forceinline__ uint4 lds128_a2(const uint8_t* p) {
+    const uint8_t* a = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+    const uint32_t sel = (reinterpret_cast<uintptr_t>(p) & 2) ? 0x5432u : 0x3210u;
+    const uint32_t w0 = lds32(a), w1 = lds32(a + 4), w2 = lds32(a + 8), w3 = lds32(a + 12),
+                   w4 = lds32(a + 16);
+    return make_uint4(prmt(w0, w1, sel), prmt(w1, w2, sel), prmt(w2, w3, sel), prmt(w3, w4, sel));
+}
+
+// Bytes of t hold (q << (7 - bits)), bit 7 clear. Float i of the word is
+// 0.5 * (1 + q_i * 2^-bits): exponent byte 0x3F with the byte as the top
+// mantissa bits.
+__device__ __forceinline__ void acc_word(uint32_t t, const float* xv, float2& s) {
+    const float f0 = __uint_as_float(prmt(t, 0x3F000000u, 0x7044u));
+    const float f1 = __uint_as_float(prmt(t, 0x3F000000u, 0x7144u));
+    const float f2 = __uint_as_float(prmt(t, 0x3F000000u, 0x7244u));
+    const float f3 = __uint_as_float(prmt(t, 0x3F000000u, 0x7344u));
+    s = ffma2(make_float2(f0, f1), make_float2(xv[0], xv[1]), s);
+    s = ffma2(make_float2(f2, f3), make_float2(xv[2], xv[3]), s);
+}
+
+// Signed int8 bytes of w -> exact q, accumulated as sum q*x.
+__device__ __forceinline__ void acc_word_s8(uint32_t w, const float* xv, float2& s) {
+    const uint32_t u = w ^ 0x80808080u;  // biased: u = q + 128
+    const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+    float2 a = make_float2(__uint_as_float(prmt(u, 0x4B000000u, 0x7440u)),
+                           __uint_as_float(prmt(u, 0x4B000000u, 0x7441u)));
+    float2 b = make_float2(__uint_as_float(prmt(u, 0x4B000000u, 0x7442u)),
+                           __uint_as_float(prmt(u, 0x4B000000u, 0x7443u)));
+    a = fadd2(a, bias);
+    b = fadd2(b, bias);
+    s = ffma2(a, make_float2(xv[0], xv[1]), s);
+    s = ffma2(b, make_float2(xv[2], xv[3]), s);
+}
+
+__device__ __forceinline__ float hsum(float2 v) { return v.x + v.y; }
+
+// Contribution of quarter c of one unit of one row: sum over the quarter's
+// 64 weights of deq(w) * x. `u` points at the unit in shared memory, `xr` are
+// the quarter's activations in decode order and `xs` their partial sums.
+template <int QT>
+__device__ __forceinline__ float unit_dot(const uint8_t* u, int c, const float* xr, const float* xs);
+
+template <>
+__device__ __forceinline__ float unit_dot<kQ4_K>(const uint8_t* u, int c, const float* xr, const float* xs) {
+    const uint4 h = lds128(u);
+    const uint4 qa = lds128(u + 16 + 32 * c);
+    const uint4 qb = lds128(u + 32 + 32 * c);
+    // scale / min pairs of sub-blocks 2c and 2c+1 (two bytes each)
+    const int hi = c >> 1;
+    const uint32_t s = 16u * (c & 1);
+    const uint32_t sc2 = hi ? (((h.w >> s) & 0x0F0Fu) | ((h.y >> (s + 2)) & 0x3030u)) : ((h.y >> s) & 0x3F3Fu);
+    const uint32_t m2 = hi ? (((h.w >> (s + 4)) & 0x0F0Fu) | ((h.z >> (s + 2)) & 0x3030u)) : ((h.z >> s) & 0x3F3Fu);
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        acc_word((q[t] << 3) & 0x78787878u, xr + 4 * t, s0);
+        acc_word((q[t] >> 1) & 0x78787878u, xr + 32 + 4 * t, s1);
+    }
+    const float u0 = fmaf(32.f, hsum(s0), -16.f * xs[0]);
+    const float u1 = fmaf(32.f, hsum(s1), -16.f * xs[1]);
+    const float accd = fmaf(static_cast<float>(sc2 & 0xFF), u0, static_cast<float>(sc2 >> 8) * u1);
+    const float accm = fmaf(static_cast<float>(m2 & 0xFF), xs[0], static_cast<float>(m2 >> 8) * xs[1]);
+    return fmaf(d, accd, -dmin * accm);
+}
+
+template <>
+__device__ __forceinline__ float unit_dot<kQ5_K>(const uint8_t* u, int c, const float* xr, const float* xs) {
+    const uint4 h = lds128(u);
+    const uint4 ha = lds128(u + 16), hb = lds128(u + 32);   // qh, shared by the 4 quarters
+    const uint4 qa = lds128(u + 48 + 32 * c);
+    const uint4 qb = lds128(u + 64 + 32 * c);
+    const int hi = c >> 1;
+    const uint32_t s = 16u * (c & 1);
+    const uint32_t sc2 = hi ? (((h.w >> s) & 0x0F0Fu) | ((h.y >> (s + 2)) & 0x3030u)) : ((h.y >> s) & 0x3F3Fu);
+    const uint32_t m2 = hi ? (((h.w >> (s + 4)) & 0x0F0Fu) | ((h.z >> (s + 2)) & 0x3030u)) : ((h.z >> s) & 0x3F3Fu);
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    const uint32_t qh[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+    const uint32_t sh = 2u * c;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const uint32_t hv = qh[t] >> sh;
+        // byte = q << 2 with q = nibble | (high bit << 4)
+        acc_word(((q[t] << 2) & 0x3C3C3C3Cu) | ((hv << 6) & 0x40404040u), xr + 4 * t, s0);
+        acc_word(((q[t] >> 2) & 0x3C3C3C3Cu) | ((hv << 5) & 0x40404040u), xr + 32 + 4 * t, s1);
+    }
+    const float u0 = fmaf(64.f, hsum(s0), -32.f * xs[0]);
+    const float u1 = fmaf(64.f, hsum(s1), -32.f * xs[1]);
+    const float accd = fmaf(static_cast<float>(sc2 & 0xFF), u0, static_cast<float>(sc2 >> 8) * u1);
+    const float accm = fmaf(static_cast<float>(m2 & 0xFF), xs[0], static_cast<float>(m2 >> 8) * xs[1]);
+    return fmaf(d, accd, -dmin * accm);
+}
+
+template <>
+__device__ __forceinline__ float unit_dot<kQ6_K>(const uint8_t* u, int c, const float* xr, const float* xs) {
+    // quarter c: half h = c>>1, positions l in [16*s2, 16*s2+16) of each of the
+    // four 32-weight groups of that half
+    const int h = c >> 1, s2 = c & 1;
+    const uint4 qa = lds128_a2(u + 64 * h + 16 * s2);
+    const uint4 qb = lds128_a2(u + 64 * h + 32 + 16 * s2);
+    const uint4 qv = lds128_a2(u + 128 + 32 * h + 16 * s2);
+    const uint8_t* scp = u + 192 + 8 * h + s2;
+    const float sc0 = static_cast<float>(static_cast<int8_t>(scp[0]));
+    const float sc1 = static_cast<float>(static_cast<int8_t>(scp[2]));
+    const float sc2 = static_cast<float>(static_cast<int8_t>(scp[4]));
+    const float sc3 = static_cast<float>(static_cast<int8_t>(scp[6]));
+    const float d = h2f_bytes(u + 208);
+    float2 g0 = make_float2(0.f, 0.f), g1 = g0, g2 = g0, g3 = g0;
+    const uint32_t a[4] = {qa.x, qa.y, qa.z, qa.w};
+    const uint32_t b[4] = {qb.x, qb.y, qb.z, qb.w};
+    const uint32_t v[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        // byte = q << 1 with q = nibble | (two high bits << 4)
+        acc_word(((a[t] << 1) & 0x1E1E1E1Eu) | ((v[t] << 5) & 0x60606060u), xr + 4 * t, g0);
+        acc_word(((b[t] << 1) & 0x1E1E1E1Eu) | ((v[t] << 3) & 0x60606060u), xr + 16 + 4 * t, g1);
+        acc_word(((a[t] >> 3) & 0x1E1E1E1Eu) | ((v[t] << 1) & 0x60606060u), xr + 32 + 4 * t, g2);
+        acc_word(((b[t] >> 3) & 0x1E1E1E1Eu) | ((v[t] >> 1) & 0x60606060u), xr + 48 + 4 * t, g3);
+    }
+    // sum (q - 32) x = 128 S - 64 X - 32 X
+    float acc = sc0 * fmaf(128.f, hsum(g0), -96.f * xs[0]);
+    acc = fmaf(sc1, fmaf(128.f, hsum(g1), -96.f * xs[1]), acc);
+    acc = fmaf(sc2, fmaf(128.f, hsum(g2), -96.f * xs[2]), acc);
+    acc = fmaf(sc3, fmaf(128.f, hsum(g3), -96.f * xs[3]), acc);
+    return d * acc;
+}
+
+template <>
+__device__ __forceinline__ float unit_dot<kQ4_0>(const uint8_t* u, int c, const float* xr, const float* xs) {
+    // quarter c = blocks 2c and 2c+1: 36 bytes at 36c (4-byte aligned)
+    const uint8_t* p = u + 36 * c;
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) w[i] = lds32(p + 4 * i);
+    const float d0 = half_bits_to_float(w[0]);
+    const float d1 = half_bits_to_float(w[4] >> 16);
+    const uint32_t q0[4] = {prmt(w[0], w[1], 0x5432u), prmt(w[1], w[2], 0x5432u),
+                            prmt(w[2], w[3], 0x5432u), prmt(w[3], w[4], 0x5432u)};
+    const uint32_t q1[4] = {w[5], w[6], w[7], w[8]};
+    float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        // byte j low nibble -> weight j, high nibble -> weight j + 16
+        acc_word((q0[t] << 3) & 0x78787878u, xr + 4 * t, s0);
+        acc_word((q0[t] >> 1) & 0x78787878u, xr + 16 + 4 * t, s0);
+        acc_word((q1[t] << 3) & 0x78787878u, xr + 32 + 4 * t, s1);
+        acc_word((q1[t] >> 1) & 0x78787878u, xr + 48 + 4 * t, s1);
+    }
+    // sum (q - 8) x = 32 S - 16 X - 8 X
+    return fmaf(d0, fmaf(32.f, hsum(s0), -24.f * xs[0]), d1 * fmaf(32.f, hsum(s1), -24.f * xs[1]));
+}
+
+template <>
+__device__ __forceinline__ float unit_dot<kQ8_0>(const uint8_t* u, int c, const float* xr, const float*) {
+    // quarter c = blocks 2c and 2c+1: 68 bytes at 68c (4-byte aligned)
+    const uint8_t* p = u + 68 * c;
+    uint32_t w[17];
+#pragma unroll
+    for (int i = 0; i < 17; ++i) w[i] = lds32(p + 4 * i);
+    const float d0 = half_bits_to_float(w[0]);
+    const float d1 = half_bits_to_float(w[8] >> 16);
+    float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        acc_word_s8(prmt(w[t], w[t + 1], 0x5432u), xr + 4 * t, s0);
+        acc_word_s8(w[9 + t], xr + 32 + 4 * t, s1);
+    }
+    return fmaf(d0, hsum(s0), d1 * hsum(s1));
+}
+
+struct StepPlan {
+    int g;       // row group
+    int u0;      // first unit
+    int n;       // units in the step (1..8)
+};
+
+__device__ __forceinline__ StepPlan plan_step(int64_t c, int64_t c_end, int units_per_row) {
+    StepPlan s;
+    s.g = static_cast<int>(c / units_per_row);
+    s.u0 = static_cast<int>(c - static_cast<int64_t>(s.g) * units_per_row);
+    const int64_t left = c_end - c;
+    int n = units_per_row - s.u0;
+    if (n > kUnitsPerStep) n = kUnitsPerStep;
+    if (left < n) n = static_cast<int>(left);
+    s.n = n;
+    return s;
+}
+
+// Warp that owns cell c when C cells are split over W warps as [wC/W, (w+1)C/W).
+// With W <= C every warp owns at least one cell.
+__device__ __forceinline__ int64_t owner_warp(int64_t c, int64_t C, int64_t W) {
+    return ((c + 1) * W - 1) / C;
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kThreads, 1)
+qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
+                  float* __restrict__ y, float scale, int* __restrict__ counters,
+                  float* __restrict__ partials, int n_stages, int* __restrict__ status) {
+    constexpr int UB = unit_bytes(QT);
+    constexpr int SLOT = slot_bytes(QT);
+    constexpr int STAGE = stage_bytes(QT);
+    extern __shared__ __align__(128) uint8_t smem[];
+
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int U = k >> 8;                                     // units per row
+    const int G = (n_out + kRows - 1) / kRows;               // row groups
+    const int64_t C = static_cast<int64_t>(G) * U;           // cells
+    const int64_t W = static_cast<int64_t>(gridDim.x) * kWarps;
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+    const int64_t c_begin = gw * C / W, c_end = (gw + 1) * C / W;
+    const size_t pitch = static_cast<size_t>(U) * UB;
+    const size_t total_bytes = pitch * static_cast<size_t>(n_out);
+    const size_t total_floor16 = total_bytes & ~size_t(15);
+
+    // shared memory: [x: U*4*kXStride f32][xsum: U*4*4 f32][stages][mbarriers]
+    float* xs_smem = reinterpret_cast<float*>(smem);
+    float* xsum_smem = xs_smem + static_cast<size_t>(U) * 4 * kXStride;
+    uint8_t* stage_base = reinterpret_cast<uint8_t*>(xsum_smem + static_cast<size_t>(U) * 16);
+    uint8_t* my_stages = stage_base + static_cast<size_t>(warp) * n_stages * STAGE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stage_base + static_cast<size_t>(kWarps) * n_stages * STAGE) +
+                     warp * kMaxStages;
+
+    if (lane == 0) {
+        for (int s = 0; s < n_stages; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    // ---- producer (lane 0): copy the kRows row segments of one step ----
+    auto issue = [&](const StepPlan& sp, int stage) {
+        uint8_t* dst = my_stages + stage * STAGE;
+        uint32_t tx = 0;
+        const uint8_t* srcs[kRows];
+        uint32_t lens[kRows];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            lens[r] = 0;
+            srcs[r] = nullptr;
+            const int row = sp.g * kRows + r;
+            if (row >= n_out) continue;
+            const size_t start = static_cast<size_t>(row) * pitch + static_cast<size_t>(sp.u0) * UB;
+            const size_t end = start + static_cast<size_t>(sp.n) * UB;
+            const size_t a0 = start & ~size_t(15);
+            size_t a1 = (end + 15) & ~size_t(15);
+            if (a1 > total_floor16) {
+                // the last < 16 bytes of W: plain loads, never past the buffer
+                a1 = total_floor16 > a0 ? total_floor16 : a0;
+                for (size_t b = a1; b < end; ++b) dst[r * SLOT + (b - a0)] = w[b];
+            }
+            srcs[r] = w + a0;
+            lens[r] = static_cast<uint32_t>(a1 - a0);
+            tx += lens[r];
+        }
+        mbar_arrive_expect_tx(&bars[stage], tx);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+            if (lens[r]) bulk_g2s(dst + r * SLOT, srcs[r], lens[r], &bars[stage]);
+    };
+
+    // Prime the ring before staging x so the copies overlap the staging.
+    int64_t prod_c = c_begin;
+    int prod_step = 0;
+    if (lane == 0) {
+        while (prod_step < n_stages && prod_c < c_end) {
+            const StepPlan sp = plan_step(prod_c, c_end, U);
+            issue(sp, prod_step);
+            prod_c += sp.n;
+            ++prod_step;
+        }
+    }
+
+    // ---- stage x (permuted, padded) and the per-quarter partial sums ----
+    for (int p0 = warp * 32; p0 < k; p0 += kThreads) {
+        const int p = p0 + lane;
+        const float v = x[p];
+        const int unit = p >> 8;
+        int c, i;
+        unit_pos_to_slot<QT>(p & 255, c, i);
+        xs_smem[(unit * 4 + c) * kXStride + i] = v;
+        float sum = v;
+        if constexpr (QT == kQ6_K) {
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if ((lane & 15) == 0) xsum_smem[(unit * 4 + c) * 4 + (i >> 4)] = sum;
+        } else {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) xsum_smem[(unit * 4 + c) * 4 + (i >> 5)] = sum;
+        }
+    }
+    __syncthreads();
+
+    // ---- consumer: all lanes ----
+    const int ju = lane >> 2;   // unit within the step
+    const int qc = lane & 3;    // quarter within the unit
+    float acc[kRows];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+
+    bool failed = false;
+    int64_t cons_c = c_begin;
+    int cons_step = 0;
+    while (cons_c < c_end) {
+        const StepPlan sp = plan_step(cons_c, c_end, U);
+        const int stage = cons_step % n_stages;
+        const uint32_t parity = static_cast<uint32_t>(cons_step / n_stages) & 1u;
+        // every lane waits; the warp leaves together if any lane gave up
+        const bool landed = mbar_wait_bounded(&bars[stage], parity, status, kStatusWaitTimeout);
+        if (!__all_sync(0xffffffffu, landed)) {
+            failed = true;
+            break;
+        }
+        const uint8_t* st = my_stages + stage * STAGE;
+        if (ju < sp.n) {
+            const int unit = sp.u0 + ju;
+            float xr[64];
+            const float4* xsrc = reinterpret_cast<const float4*>(xs_smem + (unit * 4 + qc) * kXStride);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                const float4 v = xsrc[t];
+                xr[4 * t] = v.x; xr[4 * t + 1] = v.y; xr[4 * t + 2] = v.z; xr[4 * t + 3] = v.w;
+            }
+            const float4 xsv = *reinterpret_cast<const float4*>(xsum_smem + (unit * 4 + qc) * 4);
+            const float xsum[4] = {xsv.x, xsv.y, xsv.z, xsv.w};
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                const int row = sp.g * kRows + r;
+                if (row < n_out) {
+                    const size_t start = static_cast<size_t>(row) * pitch + static_cast<size_t>(sp.u0) * UB;
+                    const uint8_t* up = st + r * SLOT + (start & 15) + ju * UB;
+                    acc[r] += unit_dot<QT>(up, qc, xr, xsum);
+                }
+            }
+        }
+        __syncwarp();
+        cons_c += sp.n;
+        ++cons_step;
+
+        // refill this stage with the step n_stages ahead
+        if (lane == 0 && prod_c < c_end) {
+            fence_proxy_async_smem();
+            const StepPlan np = plan_step(prod_c, c_end, U);
+            issue(np, stage);
+            prod_c += np.n;
+            ++prod_step;
+        }
+
+        // flush the row group when the next step leaves it (or the range ends)
+        const bool group_done = (cons_c >= c_end) || (cons_c / U != sp.g);
+        if (group_done) {
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+            }
+            const int64_t g_first = static_cast<int64_t>(sp.g) * U;
+            const int64_t g_last = g_first + U;   // exclusive
+            if (lane == 0) {
+                if (g_first >= c_begin && g_last <= c_end) {
+#pragma unroll
+                    for (int r = 0; r < kRows; ++r) {
+                        const int row = sp.g * kRows + r;
+                        if (row < n_out) y[row] = acc[r] * scale;
+                    }
+                } else {
+                    // split group: partial -> workspace, last arrival sums in warp order
+                    const int slot = (g_first <= c_begin) ? 0 : 1;   // head group : tail group
+                    float* mine = partials + (gw * 2 + slot) * kRows;
+#pragma unroll
+                    for (int r = 0; r < kRows; ++r) mine[r] = acc[r];
+                    const int64_t w_first = owner_warp(g_first, C, W);
+                    const int64_t w_last = owner_warp(g_last - 1, C, W);
+                    const int n_parts = static_cast<int>(w_last - w_first + 1);
+                    cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[sp.g]);
+                    const int prev = cnt.fetch_add(1, cuda::memory_order_acq_rel);
+                    if (prev == n_parts - 1) {
+                        float tot[kRows];
+#pragma unroll
+                        for (int r = 0; r < kRows; ++r) tot[r] = 0.f;
+                        for (int64_t ow = w_first; ow <= w_last; ++ow) {
+                            const int64_t oc0 = ow * C / W;
+                            const int oslot = (ow == w_first && oc0 / U != sp.g) ? 1 : 0;
+                            const float* pp = partials + (ow * 2 + oslot) * kRows;
+#pragma unroll
+                            for (int r = 0; r < kRows; ++r) tot[r] += pp[r];
+                        }
+#pragma unroll
+                        for (int r = 0; r < kRows; ++r) {
+                            const int row = sp.g * kRows + r;
+                            if (row < n_out) y[row] = tot[r] * scale;
+                        }
+                        cnt.store(0, cuda::memory_order_relaxed);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+        }
+    }
+
+    if (failed && lane == 0) {
+        // drain: wait (bounded) for every copy this warp still has in flight
+        for (int s = cons_step; s < prod_step; ++s) {
+            if (!mbar_wait_bounded(&bars[s % n_stages], static_cast<uint32_t>(s / n_stages) & 1u, status,
+                                   kStatusDrainTimeout))
+                break;
+        }
+    }
+}
+
+// Generic kernel for shapes the streaming kernel does not take (k not a
+// multiple of 256, W not 16-byte aligned, tiny matrices): one warp per row,
+// exact per-weight decode from global memory, fp32 FMA, shuffle reduction.
+template <int QT>
+__global__ void __launch_bounds__(256)
+qmv_rowwise_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
+                   int64_t ldx, int batch, float* __restrict__ y, int64_t ldy, float scale) {
+    constexpr int BE = block_elems(QT), BB = block_bytes(QT);
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    if (row >= n_out) return;
+    const uint8_t* wr = w + row * static_cast<int64_t>(k / BE) * BB;
+    for (int b = 0; b < batch; ++b) {
+        const float* xb = x + b * ldx;
+        float acc = 0.f;
+        for (int i = lane; i < k; i += 32) acc = fmaf(deq_weight<QT>(wr + (i / BE) * BB, i % BE), xb[i], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) y[b * ldy + row] = acc * scale;
+    }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(256)
+dequant_kernel(const uint8_t* __restrict__ w, int64_t n_rows, int64_t k, float* __restrict__ out, int64_t ldo) {
+    constexpr int BE = block_elems(QT), BB = block_bytes(QT);
+    const int64_t total = n_rows * k;
+    const int64_t nb = k / BE;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = e / k, i = e - r * k;
+        const uint8_t* blk = w + (r * nb + i / BE) * BB;
+        out[r * ldo + i] = deq_weight<QT>(blk, static_cast<int>(i % BE));
+    }
+}
+
+int g_num_sms[64] = {0};
+int* g_status_ptr[64] = {nullptr};
+
+int device_sms() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev < 0 || dev >= 64) return 148;
+    if (g_num_sms[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_num_sms[dev] = n;
+    }
+    return g_num_sms[dev];
+}
+
+// Device address of g_hesa_status for the current device (looked up once).
+cudaError_t status_ptr(int** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!g_status_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_hesa_status);
+        if (e != cudaSuccess) return e;
+        g_status_ptr[dev] = static_cast<int*>(p);
+    }
+    *out = g_status_ptr[dev];
+    return cudaSuccess;
+}
+
+template <int QT>
+cudaError_t launch_stream(const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
+                          int* counters, float* partials, int grid, cudaStream_t stream) {
+    const int U = k >> 8;
+    const size_t x_bytes = static_cast<size_t>(U) * 4 * kXStride * 4 + static_cast<size_t>(U) * 16 * 4;
+    const size_t per_stage = static_cast<size_t>(kWarps) * stage_bytes(QT);
+    const size_t bar_bytes = static_cast<size_t>(kWarps) * kMaxStages * 8;
+    if (x_bytes + per_stage + bar_bytes > static_cast<size_t>(kMaxSmem)) return cudaErrorInvalidValue;
+    int n_stages = static_cast<int>((kMaxSmem - x_bytes - bar_bytes) / per_stage);
+    if (n_stages > kMaxStages) n_stages = kMaxStages;
+    const size_t smem = x_bytes + n_stages * per_stage + bar_bytes;
+    cudaError_t e = cudaFuncSetAttribute(qmv_stream_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    int* status = nullptr;
+    e = status_ptr(&status);
+    if (e != cudaSuccess) return e;
+    qmv_stream_kernel<QT><<<grid, kThreads, smem, stream>>>(w, n_out, k, x, y, scale, counters, partials,
+                                                            n_stages, status);
+    return cudaGetLastError();
+}
+
+template <int QT>
+cudaError_t launch_rowwise(const uint8_t* w, int n_out, int k, const float* x, int64_t ldx, int batch, float* y,
+                           int64_t ldy, float scale, cudaStream_t stream) {
+    const int grid = (n_out + 7) / 8;
+    qmv_rowwise_kernel<QT><<<grid, 256, 0, stream>>>(w, n_out, k, x, ldx, batch, y, ldy, scale);
+    return cudaGetLastError();
+}
+
+template <int QT>
+cudaError_t launch_dequant(const uint8_t* w, int64_t n_rows, int64_t k, float* out, int64_t ldo,
+                           cudaStream_t stream) {
+    const int64_t total = n_rows * k;
+    int64_t blocks = (total + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(device_sms()) * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    dequant_kernel<QT><<<static_cast<int>(blocks), 256, 0, stream>>>(w, n_rows, k, out, ldo);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// host entry points (called by the C ABI)
+// ---------------------------------------------------------------------------
+
+size_t qmv_workspace_bytes(int n_out) {
+    const size_t groups = (static_cast<size_t>(n_out) + kRows - 1) / kRows;
+    const size_t counters = ((groups * sizeof(int)) + 255) & ~size_t(255);
+    const size_t partials = static_cast<size_t>(kMaxGridCtas) * kWarps * 2 * kRows * sizeof(float);
+    return counters + partials;
+}
+
+bool qmv_stream_eligible(const void* w, int64_t n_out, int64_t k) {
+    const int64_t cells = ((n_out + kRows - 1) / kRows) * (k / 256);
+    // every warp of the grid must own at least one cell (the split-group
+    // combine counts every warp between the first and the last owner)
+    return (k % 256 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0) && cells >= kWarps &&
+           k <= 32768 && n_out < (int64_t(1) << 30);
+}
+
+int qmv_stream_grid(int64_t n_out, int64_t k) {
+    const int64_t cells = ((n_out + kRows - 1) / kRows) * (k / 256);
+    // at least ~4 cells per warp so the per-step overhead amortises, and never
+    // more warps than cells
+    int64_t grid = device_sms();
+    const int64_t want = (cells + 4 * kWarps - 1) / (4 * kWarps);
+    if (want < grid) grid = want;
+    if (grid * kWarps > cells) grid = cells / kWarps;
+    if (grid < 1) grid = 1;
+    if (grid > kMaxGridCtas) grid = kMaxGridCtas;
+    return static_cast<int>(grid);
+}
+
+cudaError_t qmv_stream(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
+                       float scale, void* workspace, cudaStream_t stream, int grid_override) {
+    const size_t groups = (static_cast<size_t>(n_out) + kRows - 1) / kRows;
+    int* counters = static_cast<int*>(workspace);
+    float* partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                               (((groups * sizeof(int)) + 255) & ~size_t(255)));
+    int grid = grid_override > 0 ? grid_override : qmv_stream_grid(n_out, k);
+    const int64_t cells = static_cast<int64_t>(groups) * (k / 256);
+    if (static_cast<int64_t>(grid) * kWarps > cells) grid = static_cast<int>(cells / kWarps);
+    if (grid < 1 || grid > kMaxGridCtas) return cudaErrorInvalidValue;
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const int n = static_cast<int>(n_out), kk = static_cast<int>(k);
+    switch (qtype) {
+        case kQ4_0: return launch_stream<kQ4_0>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ8_0: return launch_stream<kQ8_0>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ4_K: return launch_stream<kQ4_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ5_K: return launch_stream<kQ5_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ6_K: return launch_stream<kQ6_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,
+                        int64_t batch, float* y, int64_t ldy, float scale, cudaStream_t stream) {
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const int n = static_cast<int>(n_out), kk = static_cast<int>(k), b = static_cast<int>(batch);
+    switch (qtype) {
+        case kQ4_0: return launch_rowwise<kQ4_0>(wb, n, kk, x, ldx, b, y, ldy, scale, stream);
+        case kQ8_0: return launch_rowwise<kQ8_0>(wb, n, kk, x, ldx, b, y, ldy, scale, stream);
+        case kQ4_K: return launch_rowwise<kQ4_K>(wb, n, kk, x, ldx, b, y, ldy, scale, stream);
+        case kQ5_K: return launch_rowwise<kQ5_K>(wb, n, kk, x, ldx, b, y, ldy, scale, stream);
+        case kQ6_K: return launch_rowwise<kQ6_K>(wb, n, kk, x, ldx, b, y, ldy, scale, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t read_device_status(int* out) {
+    return cudaMemcpyFromSymbol(out, g_hesa_status, sizeof(int));
+}
+
+cudaError_t clear_device_status(cudaStream_t stream) {
+    static const int zero = 0;
+    cudaError_t e = cudaMemcpyToSymbolAsync(g_hesa_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return e;
+    return cudaStreamSynchronize(stream);
+}
+
+cudaError_t dequantize(int qtype, const void* w, int64_t n_rows, int64_t k, float* out, int64_t ldo,
+                       cudaStream_t stream) {
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    switch (qtype) {
+        case kQ4_0: return launch_dequant<kQ4_0>(wb, n_rows, k, out, ldo, stream);
+        case kQ8_0: return launch_dequant<kQ8_0>(wb, n_rows, k, out, ldo, stream);
+        case kQ4_K: return launch_dequant<kQ4_K>(wb, n_rows, k, out, ldo, stream);
+        case kQ5_K: return launch_dequant<kQ5_K>(wb, n_rows, k, out, ldo, stream);
+        case kQ6_K: return launch_dequant<kQ6_K>(wb, n_rows, k, out, ldo, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace hesa_cuda

@@ -1,0 +1,34 @@
+// qmatvec.h -- host-side launchers of the matvec and dequant kernels
+// (implemented in qmatvec.cu, called by abi.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace hesa_cuda {
+
+// Upper bound on CTAs of the streaming kernel; sizes the workspace.
+constexpr int kMaxGridCtas = 1024;
+
+size_t qmv_workspace_bytes(int n_out);
+bool qmv_stream_eligible(const void* w, int64_t n_out, int64_t k);
+int qmv_stream_grid(int64_t n_out, int64_t k);
+
+// Batch-1 streaming matvec on CUDA cores. workspace: qmv_workspace_bytes(n_out)
+// bytes, zero-filled before first use (left zero-filled on success).
+cudaError_t qmv_stream(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
+                       float scale, void* workspace, cudaStream_t stream, int grid_override);
+
+// One warp per row, any k that is a multiple of the block size.
+cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,
+                        int64_t batch, float* y, int64_t ldy, float scale, cudaStream_t stream);
+
+// Sticky status word of the bounded waits (0 = healthy).
+cudaError_t read_device_status(int* out);
+cudaError_t clear_device_status(cudaStream_t stream);
+
+cudaError_t dequantize(int qtype, const void* w, int64_t n_rows, int64_t k, float* out, int64_t ldo,
+                       cudaStream_t stream);
+
+}  // namespace hesa_cuda
