@@ -1,0 +1,488 @@
+"""Benchmark of the GGUF quantized matvec (decode hot path) on B200.
+
+Workload (one step): the per-type matvec sweep -- W [4096 x 11008] and
+[11008 x 4096] ([n_out x k]) in each of Q8_0, Q4_K, Q5_K and Q6_K, weights fp32
+N(0, 0.02) quantized from fixed seeds, activations fp32 N(0, 1), batch 1:
+eight matvecs, 282 MB of packed weights per step. The weight set is larger
+than the 126 MB L2, so consecutive launches stream from HBM (no flush).
+
+Metric: algorithmic bytes (packed W + x + y) per second, whole job.
+  value      device time of exactly K steps replayed from a CUDA graph, inputs
+             resident in HBM (CUDA events, max over ranks).
+  e2e        the same steps through the public API (hesa_cuda.qmatvec ->
+             C ABI) with x copied from pinned host memory and y read back
+             every step.
+  roofline   achieved GB/s of the streaming kernels vs the measured HBM copy
+             peak (MEASURED_PEAKS.json).
+  cpu_baseline  the reference's own scalar matmul (cpu_matmul_f32,
+             oracle/_ref) on the dequantized weights of a bounded row sample,
+             on all host threads, rank 0 at N=1 only.
+
+N > 1 GPUs (torchrun): weak scaling with row-sharded weights -- rank r holds
+rows [r*n, (r+1)*n) of an N-times taller matrix (its shard has the N=1 shape)
+and every step ends with one NCCL all-gather of all eight y slices, so every
+rank holds the full outputs.
+
+--impl reference: times the reference CPU path (above) on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "hesa-llm_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+SWEEP = [(name, n, k) for name in ("Q8_0", "Q4_K", "Q5_K", "Q6_K") for (n, k) in ((4096, 11008), (11008, 4096))]
+QT = {"Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+BE = {2: 32, 8: 32, 12: 256, 13: 256, 14: 256}
+BB = {2: 18, 8: 34, 12: 144, 13: 176, 14: 210}
+METRIC = "quant matvec HBM GB/s (algorithmic bytes: packed W + x + y)"
+L2_NOTE = "inputs larger than L2: 282 MB weight set per step vs 126 MB L2, no flush"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def row_bytes(qt, k):
+    return (k // BE[qt]) * BB[qt]
+
+
+def step_bytes(world=1):
+    """Algorithmic bytes of one step for ONE rank's shards."""
+    tot = 0
+    for name, n, k in SWEEP:
+        tot += n * row_bytes(QT[name], k) + 4 * k + 4 * n
+    return tot
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """Per-step DRAM bytes of the streaming kernels from the committed ncu
+    summary (profiles/qmv_stream_sweep_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "qmv_stream_sweep_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    return d.get("dram_bytes_per_step")
+
+
+# --------------------------------------------------------------------------
+# clocks sampled with nvidia-smi while the GPU is under this workload
+# --------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# inputs
+# --------------------------------------------------------------------------
+
+def make_inputs(rank: int):
+    from oracle import oracle as O  # seeded generator + quantizer (input prep only, outside timing)
+    mats = []
+    for i, (name, n, k) in enumerate(SWEEP):
+        qt = QT[name]
+        w = O.quantize(qt, O.gaussian((n, k), 0.02, 1000 * (rank + 1) + i))
+        x = O.gaussian((k,), 1.0, 500 + i)
+        mats.append((name, qt, n, k, w, x))
+    return mats
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the reference's own scalar matmul on dequantized weights
+# --------------------------------------------------------------------------
+
+def cpu_reference_rate(mats, target_seconds: float = 10.0, max_pass_seconds: float | None = None,
+                       passes: int | None = None):
+    """GB/s of the reference's scalar matmul over the sweep, in the same
+    algorithmic-byte metric. A pass covers the first `rows` rows of each of
+    the eight matrices (all rows unless one pass would exceed
+    max_pass_seconds); passes repeat until target_seconds of CPU time."""
+    import ctypes
+    from oracle import oracle as O
+    ref = O.ref_lib()
+    if ref is None:
+        return None
+    threads = O.n_threads_default()
+    f32p = ctypes.POINTER(ctypes.c_float)
+
+    def prep(rows_cap):
+        out = []
+        for name, qt, n, k, w, x in mats:
+            rows = min(rows_cap, n)
+            deq = O.dequantize(qt, w[:rows], k)     # the reference stores F32 weights
+            out.append((qt, rows, k, deq, np.ascontiguousarray(x), np.empty(rows, np.float32)))
+        return out
+
+    def one_pass(samples):
+        for qt, rows, k, deq, x, y in samples:
+            ref.ref_cpu_matvec_mt(deq.ctypes.data_as(f32p), x.ctypes.data_as(f32p), y.ctypes.data_as(f32p),
+                                  rows, k, ctypes.c_float(1.0), threads)
+
+    rows_cap = 1 << 30
+    samples = prep(256)
+    t0 = time.perf_counter()
+    one_pass(samples)
+    t_small = time.perf_counter() - t0
+    full_rows = max(n for _, _, n, _, _, _ in mats)
+    est_full = t_small * full_rows / 256
+    if max_pass_seconds is not None and est_full > max_pass_seconds:
+        rows_cap = max(64, int(256 * max_pass_seconds / max(t_small, 1e-9)))
+    samples = prep(rows_cap)
+    qbytes = sum(rows * row_bytes(qt, k) + 4 * k + 4 * rows for qt, rows, k, _, _, _ in samples)
+    one_pass(samples)  # warm
+    if passes is None:
+        t0 = time.perf_counter()
+        one_pass(samples)
+        t1 = time.perf_counter() - t0
+        passes = max(1, int(target_seconds / max(t1, 1e-9)))
+    t0 = time.perf_counter()
+    for _ in range(passes):
+        one_pass(samples)
+    dt = time.perf_counter() - t0
+    rows_desc = "all rows" if rows_cap >= full_rows else f"the first {rows_cap} rows"
+    return {"value": qbytes * passes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": f"hesa::cpu_matmul_f32 (reference scalar kernel; fp32 weights dequantized outside the "
+                      f"timed region) over {rows_desc} of each of the 8 sweep matrices, {passes} pass(es), "
+                      f"rows split over {threads} host threads, {dt:.1f} s",
+            "seconds": dt, "passes": passes}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    mats = make_inputs(0)
+    # one step = one pass of the reference kernel over a row sample sized so
+    # the K timed steps take at most ~2 minutes
+    budget = max(0.05, 120.0 / max(args.steps, 1))
+    base = cpu_reference_rate(mats, max_pass_seconds=budget, passes=args.steps)
+    if base is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference CPU library (oracle/_ref) not built"}))
+        return 0
+    per_step_ms = base["seconds"] / args.steps * 1e3
+    out = {"metric": METRIC, "value": round(base["value"], 3), "unit": "GB/s", "impl": "reference",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic (seeded N(0,0.02) weights quantized to GGUF blocks, N(0,1) activations)",
+           "config": {"workload": "per-type matvec sweep Q8_0/Q4_K/Q5_K/Q6_K x {4096x11008, 11008x4096} "
+                                  "([n_out x k]), batch 1"},
+           "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+           "e2e": {"value": round(base["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------
+
+def run_gpu(args, rank: int, world: int, local_rank: int):
+    import torch
+    import hesa_cuda as H
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        pg = dist
+
+    H.lib()
+    mats = make_inputs(rank)
+    dmats = []
+    for name, qt, n, k, w, x in mats:
+        wt = torch.from_numpy(w).to(dev)
+        xt = torch.from_numpy(x).to(dev)
+        yt = torch.empty(n, dtype=torch.float32, device=dev)
+        ws = H.make_workspace(qt, n, k, device=dev)
+        dmats.append((name, qt, n, k, wt, xt, yt, ws))
+    # the full (all-gathered) outputs of one step
+    y_local = torch.empty(sum(n for _, _, n, _, _, _, _, _ in dmats), dtype=torch.float32, device=dev)
+    y_all = torch.empty(world * y_local.numel(), dtype=torch.float32, device=dev)
+
+    # quick parity check of every matrix on a few rows (oracle on CPU, outside timing)
+    from oracle import oracle as O
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for (name, qt, n, k, wt, xt, yt, ws), (_, _, _, _, w, x) in zip(dmats, mats):
+            H.qmatvec(qt, wt, xt, y=yt, workspace=ws)
+        stream.synchronize()
+        for (name, qt, n, k, wt, xt, yt, ws), (_, _, _, _, w, x) in zip(dmats, mats):
+            ref = O.qmatvec(qt, w[:64], x)
+            got = yt[:64].cpu().numpy()
+            err = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+            if err > 1e-5:
+                raise SystemExit(f"parity check failed for {name} {n}x{k}: rel L2 {err:.3e}")
+
+    def one_step():
+        off = 0
+        for name, qt, n, k, wt, xt, yt, ws in dmats:
+            H.qmatvec(qt, wt, xt, y=y_local[off:off + n], workspace=ws, stream=stream)
+            off += n
+        if pg is not None:
+            pg.all_gather_into_tensor(y_all, y_local)
+
+    # capture one step in a CUDA graph; replaying it removes host launch gaps
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one_step()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            one_step()
+        stream.synchronize()
+
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        stream.synchronize()
+
+        # clocks: sampled over a ~2 s load window of the same replay and the timed region
+        sampler = ClockSampler(local_rank) if rank == 0 else None
+        if sampler:
+            sampler.start()
+        t_end = time.time() + 2.0
+        while time.time() < t_end:
+            for _ in range(200):
+                graph.replay()
+            stream.synchronize()
+
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        ev1.synchronize()
+        torch.cuda.synchronize(dev)
+        dt_ms = ev0.elapsed_time(ev1)
+        clocks = sampler.stop() if sampler else None
+
+        # kernel-only time of the same step without the collective (roofline)
+        if pg is not None:
+            kgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(kgraph, stream=stream):
+                off = 0
+                for name, qt, n, k, wt, xt, yt, ws in dmats:
+                    H.qmatvec(qt, wt, xt, y=y_local[off:off + n], workspace=ws, stream=stream)
+                    off += n
+            for _ in range(3):
+                kgraph.replay()
+            stream.synchronize()
+            ek0 = torch.cuda.Event(enable_timing=True)
+            ek1 = torch.cuda.Event(enable_timing=True)
+            ek0.record(stream)
+            for _ in range(args.steps):
+                kgraph.replay()
+            ek1.record(stream)
+            ek1.synchronize()
+            kernel_ms = ek0.elapsed_time(ek1)
+        else:
+            kernel_ms = dt_ms
+
+        # per-type breakdown (kernel only): each type's two matrices are
+        # cloned until the rotated set exceeds 300 MB, so every launch streams
+        # its weights from HBM rather than L2
+        per_type = {}
+        if rank == 0:
+            for tname in ("Q8_0", "Q4_K", "Q5_K", "Q6_K"):
+                sel = [m for m in dmats if m[0] == tname]
+                pair = sum(m[4].numel() for m in sel)
+                copies = max(2, -(-300_000_000 // pair))
+                rot = [(qt, n, k, wt.clone(), xt, yt, ws) for _ in range(copies)
+                       for (name, qt, n, k, wt, xt, yt, ws) in sel]
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for qt, n, k, wt, xt, yt, ws in rot:
+                        H.qmatvec(qt, wt, xt, y=yt, workspace=ws, stream=stream)
+                for _ in range(3):
+                    g.replay()
+                stream.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                reps = 20
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
+                e1.synchronize()
+                by = sum(n * row_bytes(qt, k) + 4 * k + 4 * n for qt, n, k, _, _, _, _ in rot) * reps
+                per_type[tname] = round(by / (e0.elapsed_time(e1) * 1e-3) / 1e9, 1)
+                del g, rot
+
+        # e2e through the public API with host buffers
+        xs_host = [torch.from_numpy(x).pin_memory() for _, _, _, _, _, x in mats]
+        ys_host = [torch.empty(n, dtype=torch.float32).pin_memory() for _, _, n, _, _, _ in mats]
+        h2d = sum(x.numel() * 4 for x in xs_host)
+        d2h = sum(y.numel() * 4 for y in ys_host) + (y_all.numel() * 4 - y_local.numel() * 4 if pg else 0)
+
+        def e2e_step():
+            off = 0
+            for (name, qt, n, k, wt, xt, yt, ws), xh, yh in zip(dmats, xs_host, ys_host):
+                xt.copy_(xh, non_blocking=True)
+                H.qmatvec(qt, wt, xt, y=y_local[off:off + n], workspace=ws, stream=stream)
+                off += n
+            if pg is not None:
+                pg.all_gather_into_tensor(y_all, y_local)
+            off = 0
+            for (name, qt, n, k, wt, xt, yt, ws), yh in zip(dmats, ys_host):
+                yh.copy_(y_local[off:off + n], non_blocking=True)
+                off += n
+            stream.synchronize()
+
+        for _ in range(3):
+            e2e_step()
+        if pg is not None:
+            pg.barrier()
+        ee0 = torch.cuda.Event(enable_timing=True)
+        ee1 = torch.cuda.Event(enable_timing=True)
+        ee0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ee1.record(stream)
+        ee1.synchronize()
+        e2e_ms = ee0.elapsed_time(ee1)
+
+    # max over ranks
+    times = torch.tensor([dt_ms, kernel_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(times, op=pg.ReduceOp.MAX)
+    dt_ms, kernel_ms, e2e_ms = (float(v) for v in times.cpu())
+
+    if rank == 0:
+        bytes_step = step_bytes() * world
+        value = bytes_step * args.steps / (dt_ms * 1e-3) / 1e9
+        achieved = step_bytes() * args.steps / (kernel_ms * 1e-3) / 1e9
+        peak, peak_kind = measured_peaks()
+        traffic = committed_traffic()
+        cpu_base = None
+        if world == 1:
+            cpu_base = cpu_reference_rate(mats, target_seconds=10.0, max_pass_seconds=2.0)
+            if cpu_base:
+                cpu_base = {k: cpu_base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+                cpu_base["value"] = round(cpu_base["value"], 3)
+        out = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantized to GGUF blocks, N(0,1) activations)",
+            "config": {"workload": "per-type matvec sweep Q8_0/Q4_K/Q5_K/Q6_K x {4096x11008, 11008x4096} "
+                                   "([n_out x k]), batch 1",
+                       "bytes_per_step_per_gpu": step_bytes(), "l2": L2_NOTE,
+                       "parallelism": (f"row-sharded weights x{world}, NCCL all-gather of y" if world > 1
+                                       else "single GPU"),
+                       "timing": "CUDA graph of one step, replayed K times between CUDA events"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": traffic,
+                         "kernel": "qmv_stream_kernel (8 launches per step)"},
+            "per_type_gbs": per_type,
+            "pct_of_8tbs": round(achieved / 8000.0, 4),
+            "e2e": {"value": round(bytes_step * args.steps / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": len(SWEEP) * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu_base,
+        }
+        print(json.dumps(out), flush=True)
+
+    del graph
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="hesa", choices=["hesa", "reference"])
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus else 1)))
+    if "WORLD_SIZE" not in os.environ:
+        world = 1
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_gpu(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -571,9 +571,17 @@ cudaError_t launch_stream(const uint8_t* w, int n_out, int k, const float* x, fl
     int n_stages = static_cast<int>((kMaxSmem - x_bytes - bar_bytes) / per_stage);
     if (n_stages > kMaxStages) n_stages = kMaxStages;
     const size_t smem = x_bytes + n_stages * per_stage + bar_bytes;
-    cudaError_t e = cudaFuncSetAttribute(qmv_stream_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    // raise the kernel's dynamic shared-memory limit once per device
+    static int smem_set[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem_set[dev] < kMaxSmem) {
+        e = cudaFuncSetAttribute(qmv_stream_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        if (e != cudaSuccess) return e;
+        smem_set[dev] = kMaxSmem;
+    }
     int* status = nullptr;
     e = status_ptr(&status);
     if (e != cudaSuccess) return e;

@@ -1,0 +1,150 @@
+"""Python binding of the hesa-b200 C ABI (include/hesa_cuda.h) over ctypes.
+
+This is the host-side mirror of the reference's operator interface for the
+hot path: ``qmatvec`` is ``hesa::Backend::matmul`` (include/hesa/backend.hpp:
+43-44) for a quantized weight, with the same argument meaning (W [n_out, k],
+activations [batch, k], out = scale * W @ x) and the same error codes
+(``hesa::Error``, include/hesa/result.hpp:14-30), raised as ``HesaError``.
+
+PyTorch is only plumbing here: it owns device memory and streams. Every
+computation runs in ``libhesa_cuda.so``; if that library cannot be built or
+loaded, every call raises -- there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import hesa_build as _build
+
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 2, 8, 12, 13, 14
+QTYPES = {"Q4_0": Q4_0, "Q8_0": Q8_0, "Q4_K": Q4_K, "Q5_K": Q5_K, "Q6_K": Q6_K}
+BLOCK_ELEMS = {Q4_0: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
+
+ERRORS = {0: "SUCCESS", 1: "OUT_OF_MEMORY", 2: "INVALID_ARGUMENT", 3: "BACKEND_NOT_AVAILABLE",
+          6: "SHAPE_MISMATCH", 8: "INVALID_FORMAT", 9: "CUDA_ERROR", 14: "INTERNAL_ERROR"}
+
+# (name, restype, argtypes) of every function include/hesa_cuda.h declares
+_vp, _i64, _sz, _int, _f = ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t, ctypes.c_int, ctypes.c_float
+SIGNATURES = [
+    ("hesa_cuda_version", ctypes.c_char_p, []),
+    ("hesa_cuda_row_bytes", _sz, [_int, _i64]),
+    ("hesa_cuda_qmatvec_workspace_size", _sz, [_int, _i64, _i64, _i64]),
+    ("hesa_cuda_qmatvec", _int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _f, _vp, _sz, _vp]),
+    ("hesa_cuda_dequantize", _int, [_int, _vp, _i64, _i64, _vp, _i64, _vp]),
+    ("hesa_cuda_device_status", _int, [_vp, ctypes.POINTER(_int)]),
+    ("hesa_cuda_clear_device_status", _int, [_vp]),
+    ("hesa_cuda_last_error", ctypes.c_char_p, []),
+]
+
+
+class HesaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)} ({code}): {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def library_path() -> str:
+    return _build.CUDA_SO
+
+
+def lib() -> ctypes.CDLL:
+    """Load libhesa_cuda.so, building it first if it is missing or stale."""
+    global _lib
+    if _lib is None:
+        path = _build.build_cuda()
+        L = ctypes.CDLL(path)
+        for name, res, args in SIGNATURES:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise HesaError(rc, lib().hesa_cuda_last_error().decode())
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream or None
+    if isinstance(stream, int):
+        return stream or None
+    return stream.cuda_stream or None
+
+
+def row_bytes(qtype: int, k: int) -> int:
+    return int(lib().hesa_cuda_row_bytes(qtype, k))
+
+
+def workspace_bytes(qtype: int, n_out: int, k: int, batch: int = 1) -> int:
+    return int(lib().hesa_cuda_qmatvec_workspace_size(qtype, n_out, k, batch))
+
+
+def make_workspace(qtype: int, n_out: int, k: int, batch: int = 1, device=None):
+    """A zero-filled device workspace of the size the matvec asks for."""
+    import torch
+    nbytes = max(16, workspace_bytes(qtype, n_out, k, batch))
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device or "cuda")
+
+
+def qmatvec(qtype: int, w, x, y=None, scale: float = 1.0, workspace=None, stream=None, k: int | None = None):
+    """y = scale * W @ x for packed W [n_out, row_bytes] (uint8, CUDA) and fp32
+    x [k] or [batch, k]; returns y [n_out] or [batch, n_out]."""
+    import torch
+    squeeze = x.dim() == 1
+    x2 = x.unsqueeze(0) if squeeze else x
+    batch, kk = x2.shape
+    k = k or kk
+    n_out = w.shape[0]
+    if y is None:
+        y = torch.empty((batch, n_out), dtype=torch.float32, device=x.device)
+    y2 = y.unsqueeze(0) if y.dim() == 1 else y
+    if workspace is None:
+        workspace = make_workspace(qtype, n_out, k, batch, device=x.device)
+    rc = lib().hesa_cuda_qmatvec(qtype, w.data_ptr(), n_out, k, x2.data_ptr(), x2.stride(0), batch,
+                                 y2.data_ptr(), y2.stride(0), float(scale), workspace.data_ptr(),
+                                 workspace.numel(), _stream_handle(stream))
+    _check(rc)
+    return y2[0] if squeeze else y2
+
+
+def dequantize(qtype: int, w, k: int, out=None, stream=None):
+    import torch
+    n_rows = w.shape[0]
+    if out is None:
+        out = torch.empty((n_rows, k), dtype=torch.float32, device=w.device)
+    _check(lib().hesa_cuda_dequantize(qtype, w.data_ptr(), n_rows, k, out.data_ptr(), out.stride(0),
+                                      _stream_handle(stream)))
+    return out
+
+
+def device_status(stream=None) -> int:
+    v = ctypes.c_int(0)
+    _check(lib().hesa_cuda_device_status(_stream_handle(stream), ctypes.byref(v)))
+    return v.value
+
+
+def clear_device_status(stream=None) -> None:
+    _check(lib().hesa_cuda_clear_device_status(_stream_handle(stream)))
+
+
+def loaded_library_files() -> list[str]:
+    """Shared objects of this package mapped into the current process."""
+    out = []
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                p = line.split()[-1]
+                if p.endswith(".so") and os.path.dirname(p) == os.path.dirname(library_path()):
+                    out.append(p)
+    except OSError:
+        pass
+    return sorted(set(out))

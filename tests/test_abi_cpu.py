@@ -1,0 +1,84 @@
+"""CPU tests of the C ABI: the library builds and loads, exports every function
+include/hesa_cuda.h declares, and rejects bad arguments on the host before
+any CUDA call (so these run without a GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import hesa_cuda as H
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for hdr in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if hdr.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", hdr)).read()
+            names += re.findall(r"HESA_CUDA_API\s+[\w\s\*]+?\b(hesa_cuda_\w+)\s*\(", text)
+    return names
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert "hesa_cuda_qmatvec" in names and "hesa_cuda_dequantize" in names
+    assert sorted(names) == sorted(n for n, _, _ in H.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    L = H.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+    assert b"sm_100a" in L.hesa_cuda_version()
+
+
+@pytest.mark.parametrize("qt,k,expect", [(2, 4096, 2304), (8, 11008, 11696), (12, 11008, 6192),
+                                         (13, 4096, 2816), (14, 11008, 9030), (12, 100, 0), (3, 256, 0)])
+def test_row_bytes(qt, k, expect):
+    assert H.row_bytes(qt, k) == expect
+
+
+def test_workspace_size_is_small_and_positive():
+    ws = H.workspace_bytes(12, 11008, 4096)
+    assert 0 < ws < 2 << 20
+    assert H.workspace_bytes(3, 16, 256) == 0
+
+
+FAKE = 1 << 20  # non-null, 16-byte aligned, never dereferenced: validation fails first
+
+
+def call(qt=12, w=FAKE, n=64, k=256, x=FAKE, ldx=256, b=1, y=FAKE, ldy=64, ws=FAKE, wsb=1 << 20):
+    return H.lib().hesa_cuda_qmatvec(qt, w, n, k, x, ldx, b, y, ldy, 1.0, ws, wsb, None)
+
+
+@pytest.mark.parametrize("kwargs,code", [
+    (dict(qt=3), 3),                 # unsupported type -> BACKEND_NOT_AVAILABLE
+    (dict(w=0), 2),                  # null -> INVALID_ARGUMENT
+    (dict(x=0), 2),
+    (dict(n=0), 6),                  # SHAPE_MISMATCH
+    (dict(k=100), 6),                # not a multiple of the block
+    (dict(ldx=128), 6),
+    (dict(b=2, ldy=32), 6),
+    (dict(w=FAKE + 8), 2),           # misaligned weights
+    (dict(x=FAKE + 4), 2),           # misaligned activations
+    (dict(wsb=16), 2),               # workspace too small
+    (dict(ws=0), 2),
+])
+def test_qmatvec_rejects_bad_arguments_without_launching(kwargs, code):
+    assert call(**kwargs) == code
+    assert H.lib().hesa_cuda_last_error()
+
+
+def test_dequantize_rejects_bad_arguments():
+    L = H.lib()
+    assert L.hesa_cuda_dequantize(12, FAKE, 4, 100, FAKE, 100, None) == 6
+    assert L.hesa_cuda_dequantize(5, FAKE, 4, 256, FAKE, 256, None) == 3
+    assert L.hesa_cuda_dequantize(12, 0, 4, 256, FAKE, 256, None) == 2
+
+
+def test_error_type_carries_reference_code():
+    with pytest.raises(H.HesaError) as ei:
+        H._check(6)
+    assert ei.value.code == 6 and "SHAPE_MISMATCH" in str(ei.value)
