@@ -294,6 +294,17 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         if pg is not None:
             pg.all_gather_into_tensor(y_all, y_local)
 
+    if args.profile:
+        # a short, untimed run for ncu: K plain steps (8 launches each), no graphs
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                one_step()
+            stream.synchronize()
+        if pg is not None:
+            pg.destroy_process_group()
+        log(f"profile run done: {args.steps} step(s), {len(SWEEP) * args.steps} matvec launches")
+        return 0
+
     # capture one step in a CUDA graph; replaying it removes host launch gaps
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -473,6 +484,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="hesa", choices=["hesa", "reference"])
+    ap.add_argument("--profile", action="store_true",
+                    help="untimed: build inputs, run --steps plain steps, exit (for ncu captures)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus else 1)))
