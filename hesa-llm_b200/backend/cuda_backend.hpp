@@ -1,0 +1,86 @@
+// cuda_backend.hpp -- hesa::Backend implementation for NVIDIA B200 (sm_100a).
+//
+// The drop-in for the CUDA slot of hesa-llm: src/backend/backend.cpp:32-37
+// constructs `CudaBackend(cfg)` when HESA_HAS_CUDA is defined, and
+// CMakeLists.txt:99-100 compiles src/backend/cuda_backend.cpp. This class is
+// that backend. It implements the interface of include/hesa/backend.hpp:28-65
+// and reaches the GPU only through the C ABI of include/hesa_cuda.h.
+//
+// Tensors of the reference own host memory (src/tensor/tensor.cpp:63-77;
+// device_ptr is never set), so the backend keeps device copies itself:
+//   * weight views of a quantized dtype are uploaded once and cached by
+//     (host pointer, bytes) -- GGUF weights are immutable after Model::load;
+//   * activations and outputs travel through pinned staging buffers on every
+//     call, on the backend's own stream.
+// Calls are asynchronous on that stream except where a host result is
+// produced (matmul writes `out`, a host view); synchronize() joins.
+#pragma once
+
+#include "hesa/backend.hpp"
+
+#include <cstddef>
+#include <cstdint>
+#include <map>
+#include <utility>
+
+namespace hesa {
+
+class CudaBackend final : public Backend {
+public:
+    explicit CudaBackend(DeviceConfig cfg);
+    ~CudaBackend() override;
+
+    CudaBackend(const CudaBackend&) = delete;
+    CudaBackend& operator=(const CudaBackend&) = delete;
+
+    BackendType type() const override { return BackendType::CUDA; }
+    const char* name() const override { return "CUDA (B200 sm_100a)"; }
+    bool supports(Dtype dt) const override;
+    size_t device_memory() const override;
+    size_t device_memory_used() const override;
+
+    Result<Tensor> alloc_tensor(Dtype dtype, std::span<const int64_t> shape) override;
+    Result<void> free_tensor(Tensor& tensor) override;
+
+    // out = scale * a @ b with a = W [n_out, k] (Q4_0/Q8_0/Q4_K/Q5_K/Q6_K or
+    // F32), b = [k, batch] F32 (any byte strides, e.g. a transposed [batch, k]
+    // view), out = [n_out, batch] F32 (any byte strides).
+    Result<void> matmul(TensorView a, TensorView b, TensorView out, float scale = 1.0f) override;
+    Result<void> add(TensorView a, TensorView b, TensorView out) override;
+    Result<void> mul(TensorView a, TensorView b, TensorView out) override;
+    Result<void> softmax(TensorView in, TensorView out, int axis = -1) override;
+    Result<void> rms_norm(TensorView in, TensorView weight, TensorView out, float eps = 1e-6f) override;
+    Result<void> rope(TensorView in_out, std::span<const int32_t> positions, float freq_base,
+                      int n_dims) override;
+    Result<void> silu(TensorView in, TensorView out) override;
+    Result<void> scaled_dot_product_attention(TensorView q, TensorView k, TensorView v, TensorView out,
+                                              TensorView mask = {}, float scale = 0.0f) override;
+    Result<Tensor> quantize(TensorView src, Dtype target_dtype) override;
+    Result<void> synchronize() override;
+    Result<void> copy_tensor(const Tensor& src, Tensor& dst) override;
+
+    int device_id() const { return device_; }
+    void* stream() const { return stream_; }
+    // number of weight uploads kept on the device (test hook)
+    size_t cached_weights() const { return weights_.size(); }
+
+private:
+    struct DevBuf {
+        void* ptr = nullptr;
+        size_t bytes = 0;
+    };
+    Result<void> ensure(DevBuf& b, size_t bytes);
+    Result<void> ensure_host(DevBuf& b, size_t bytes);
+    Result<const void*> device_weights(const void* host, size_t bytes);
+    Result<void> activate() const;
+
+    int device_ = 0;
+    size_t memory_limit_ = 0;
+    void* stream_ = nullptr;
+    std::map<std::pair<const void*, size_t>, DevBuf> weights_;
+    size_t weight_bytes_ = 0;
+    DevBuf d_x_, d_y_, d_ws_, h_x_, h_y_;
+    size_t ws_zeroed_ = 0;
+};
+
+}  // namespace hesa

@@ -106,3 +106,119 @@ int hesa_cuda_clear_device_status(void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// decode-step helpers
+// ---------------------------------------------------------------------------
+
+#include "decode_ops.h"
+
+#include <cmath>
+
+extern "C" {
+
+int hesa_cuda_matmul_f32(const float* a, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
+                         float* y, int64_t ldy, float scale, void* stream) {
+    if (!a || !x || !y) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_out <= 0 || k <= 0 || batch <= 0 || ldx < k || (batch > 1 && ldy < n_out) ||
+        n_out >= (int64_t(1) << 31) || k >= (int64_t(1) << 31))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::matmul_f32(a, n_out, k, x, ldx, batch, y, ldy, scale, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "matmul_f32");
+}
+
+int hesa_cuda_rms_norm(const float* in, const float* weight, float* out, int64_t n_rows, int64_t n, float eps,
+                       void* stream) {
+    if (!in || !weight || !out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_rows <= 0 || n <= 0 || n_rows >= (int64_t(1) << 31) || n >= (int64_t(1) << 31))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::rms_norm(in, weight, out, n_rows, n, eps, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "rms_norm");
+}
+
+int hesa_cuda_silu_mul(const float* gate, const float* up, float* out, int64_t n, void* stream) {
+    if (!gate || !out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::silu_mul(gate, up, out, n, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "silu_mul");
+}
+
+int hesa_cuda_add(const float* a, const float* b, float* out, int64_t n, void* stream) {
+    if (!a || !b || !out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::binary(a, b, out, n, 0, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "add");
+}
+
+int hesa_cuda_mul(const float* a, const float* b, float* out, int64_t n, void* stream) {
+    if (!a || !b || !out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::binary(a, b, out, n, 1, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "mul");
+}
+
+int hesa_cuda_softmax(const float* in, float* out, int64_t n_rows, int64_t n, void* stream) {
+    if (!in || !out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_rows <= 0 || n <= 0 || n_rows >= (int64_t(1) << 31) || n >= (int64_t(1) << 31))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::softmax(in, out, n_rows, n, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "softmax");
+}
+
+int hesa_cuda_rope_table(float* table_host, int32_t n_pos, int64_t head_dim, float freq_base) {
+    if (!table_host) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_pos <= 0 || head_dim <= 0 || (head_dim & 1)) return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    const int64_t half = head_dim / 2;
+    for (int32_t p = 0; p < n_pos; ++p) {
+        float* row = table_host + static_cast<int64_t>(p) * head_dim;
+        for (int64_t d = 0; d < half; ++d) {
+            // the expressions of cpu_rope_f32, in float, with the host libm
+            const float freq = 1.0f / std::pow(freq_base, 2.0f * static_cast<float>(d) / static_cast<float>(head_dim));
+            const float theta = static_cast<float>(p) * freq;
+            row[d] = std::cos(theta);
+            row[half + d] = std::sin(theta);
+        }
+    }
+    return HESA_CUDA_OK;
+}
+
+int hesa_cuda_rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, const int32_t* pos_dev,
+                   int32_t pos_host, void* stream) {
+    if (!data || !table) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_heads <= 0 || head_dim <= 0 || (head_dim & 1) || (!pos_dev && pos_host < 0))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::rope(data, n_heads, head_dim, table, pos_dev, pos_host, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "rope");
+}
+
+int hesa_cuda_kv_store(const float* k, const float* v, void* k_cache, void* v_cache, int64_t row_elems, int64_t ctx,
+                       const int32_t* pos_dev, int32_t pos_host, void* stream) {
+    if (!k || !v || !k_cache || !v_cache) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (row_elems <= 0 || ctx <= 0 || (!pos_dev && pos_host < 0) || row_elems * ctx >= (int64_t(1) << 40))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::kv_store(k, v, k_cache, v_cache, row_elems, ctx, pos_dev, pos_host,
+                                        static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "kv_store");
+}
+
+size_t hesa_cuda_attention_workspace_size(int64_t n_head, int64_t head_dim, int64_t ctx) {
+    if (n_head <= 0 || head_dim <= 0 || ctx <= 0) return 0;
+    return hesa_cuda::attention_workspace_bytes(n_head, head_dim, ctx);
+}
+
+int hesa_cuda_attention(const float* q, const void* k_cache, const void* v_cache, float* out, int64_t n_head,
+                        int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+    if (!q || !k_cache || !v_cache || !out || !workspace) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_head <= 0 || n_kv_head <= 0 || n_head % n_kv_head != 0 || ctx <= 0 || (!pos_dev && pos_host < 0))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "head_dim must be 64, 128 or 256");
+    if (workspace_bytes < hesa_cuda::attention_workspace_bytes(n_head, head_dim, ctx))
+        return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace too small");
+    cudaError_t e = hesa_cuda::attention(q, k_cache, v_cache, out, n_head, n_kv_head, head_dim, ctx, pos_dev,
+                                         pos_host, workspace, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "attention");
+}
+
+}  // extern "C"

@@ -1,0 +1,343 @@
+// decode_ops.cu -- the non-matvec kernels of a Llama-style decode step
+// (single token), with the semantics of hesa-llm's CPU kernels
+// (src/backend/cpu_backend.cpp):
+//   matmul_f32    cpu_matmul_f32 (:24-41) for F32 weights, one warp per row
+//   rms_norm      cpu_rms_norm_f32 (:72-89): inv = 1/sqrt(mean(x^2) + eps)
+//   silu_mul      cpu_silu_f32 (:91-96) of gate, times up
+//   add / mul     cpu_add_f32 (:43-46) / CPU_Backend::mul (:170-177)
+//   softmax       cpu_softmax_f32 (:48-70)
+//   rope          cpu_rope_f32 (:98-120), rotate-half, angles from a table
+//                 computed on the host with the reference's own formulas
+//   kv_store      fp16 ring-buffer write of k and v at slot pos % ctx
+//   attention     single-query SDPA (:225-294) over the fp16 ring, GQA,
+//                 score scale 1/sqrt(head_dim), split over the context
+//                 with a deterministic last-arrival combine per head
+// The position is read from device memory so a captured CUDA graph can be
+// replayed for every token.
+#include "hesa_common.cuh"
+#include "decode_ops.h"
+
+#include <cuda/atomic>
+#include <cuda_fp16.h>
+
+namespace hesa_cuda {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__global__ void __launch_bounds__(256)
+matmul_f32_kernel(const float* __restrict__ a, int n_out, int k, const float* __restrict__ x, int64_t ldx,
+                  int batch, float* __restrict__ y, int64_t ldy, float scale) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    if (row >= n_out) return;
+    const float* ar = a + row * k;
+    for (int b = 0; b < batch; ++b) {
+        const float* xb = x + b * ldx;
+        float acc = 0.f;
+        for (int i = lane; i < k; i += 32) acc = fmaf(ar[i], xb[i], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) y[b * ldy + row] = acc * scale;
+    }
+}
+
+// One CTA per row.
+__global__ void __launch_bounds__(256)
+rms_norm_kernel(const float* __restrict__ in, const float* __restrict__ w, float* __restrict__ out, int n,
+                float eps) {
+    __shared__ float red[8];
+    const float* row = in + static_cast<int64_t>(blockIdx.x) * n;
+    float* o = out + static_cast<int64_t>(blockIdx.x) * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) tot += red[i];
+    const float inv = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = row[i] * inv * w[i];
+}
+
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ o,
+                                int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float v = g[i];
+        o[i] = (v / (1.0f + expf(-v))) * (u ? u[i] : 1.0f);
+    }
+}
+
+__global__ void binary_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ o,
+                              int64_t n, int op) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        o[i] = op == 0 ? a[i] + b[i] : a[i] * b[i];
+}
+
+__global__ void __launch_bounds__(256)
+softmax_kernel(const float* __restrict__ in, float* __restrict__ out, int n) {
+    __shared__ float red[8];
+    const float* row = in + static_cast<int64_t>(blockIdx.x) * n;
+    float* o = out + static_cast<int64_t>(blockIdx.x) * n;
+    const int nw = blockDim.x >> 5;
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, row[i]);
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = red[0];
+    for (int i = 1; i < nw; ++i) m = fmaxf(m, red[i]);
+    __syncthreads();
+    float s = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float e = expf(row[i] - m);
+        o[i] = e;
+        s += e;
+    }
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < nw; ++i) tot += red[i];
+    const float inv = 1.0f / tot;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] *= inv;
+}
+
+// data [n_heads, head_dim]; table row p holds cos[half] then sin[half]
+__global__ void rope_kernel(float* __restrict__ data, int n_heads, int head_dim, const float* __restrict__ table,
+                            const int32_t* __restrict__ pos_dev, int32_t pos_host) {
+    const int half = head_dim >> 1;
+    const int32_t pos = pos_dev ? *pos_dev : pos_host;
+    const float* cs = table + static_cast<int64_t>(pos) * head_dim;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_heads * half; i += gridDim.x * blockDim.x) {
+        const int h = i / half, d = i - h * half;
+        float* row = data + static_cast<int64_t>(h) * head_dim;
+        const float c = cs[d], s = cs[half + d];
+        const float x0 = row[d], x1 = row[d + half];
+        row[d] = x0 * c - x1 * s;
+        row[d + half] = x0 * s + x1 * c;
+    }
+}
+
+__global__ void kv_store_kernel(const float* __restrict__ k, const float* __restrict__ v, __half* __restrict__ kc,
+                                __half* __restrict__ vc, int row_elems, int ctx, const int32_t* __restrict__ pos_dev,
+                                int32_t pos_host) {
+    const int32_t pos = pos_dev ? *pos_dev : pos_host;
+    const int64_t slot = pos % ctx;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row_elems; i += gridDim.x * blockDim.x) {
+        kc[slot * row_elems + i] = __float2half_rn(k[i]);
+        vc[slot * row_elems + i] = __float2half_rn(v[i]);
+    }
+}
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnMaxDim = 256;
+
+// grid (n_head, n_split); 4 warps; lane owns head_dim/32 consecutive dims.
+// Each CTA reduces its context chunk to (max, sum, acc[head_dim]) and writes
+// it to the workspace; the last CTA of the head (ticket) combines the splits
+// in split order and writes out.
+template <int DPL>  // dims per lane (head_dim / 32)
+__global__ void __launch_bounds__(kAttnWarps * 32)
+attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
+                 float* __restrict__ out, int n_head, int n_kv_head, int ctx, const int32_t* __restrict__ pos_dev,
+                 int32_t pos_host, int chunk, float* __restrict__ part, int* __restrict__ counters) {
+    const int head_dim = DPL * 32;
+    const int h = blockIdx.x, split = blockIdx.y, n_split = gridDim.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int32_t pos = pos_dev ? *pos_dev : pos_host;
+    const int n_ctx = pos + 1 < ctx ? pos + 1 : ctx;
+    const int kvh = h / (n_head / n_kv_head);
+    const int64_t row_stride = static_cast<int64_t>(n_kv_head) * head_dim;
+    const float sc = 1.0f / sqrtf(static_cast<float>(head_dim));
+
+    float qv[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) qv[i] = q[static_cast<int64_t>(h) * head_dim + lane * DPL + i];
+
+    const int j0 = split * chunk;
+    const int j1 = min(n_ctx, j0 + chunk);
+    float m = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
+        const __half* kr = kc + j * row_stride + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
+        const __half* vr = vc + j * row_stride + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) s = fmaf(qv[i], __half2float(kr[i]), s);
+        s = warp_sum(s) * sc;
+        const float mn = fmaxf(m, s);
+        const float corr = expf(m - mn);   // 0 on the first position (m = -inf)
+        const float p = expf(s - mn);
+        l = l * corr + p;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, __half2float(vr[i]), acc[i] * corr);
+        m = mn;
+    }
+
+    // combine the 4 warps of the CTA
+    __shared__ float s_m[kAttnWarps], s_l[kAttnWarps];
+    __shared__ float s_acc[kAttnWarps][kAttnMaxDim];
+    if (lane == 0) {
+        s_m[warp] = m;
+        s_l[warp] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) s_acc[warp][lane * DPL + i] = acc[i];
+    __syncthreads();
+    float* mine = part + (static_cast<int64_t>(h) * n_split + split) * (head_dim + 2);
+    if (warp == 0) {
+        float M = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w]);
+        float L = 0.f;
+        float a[DPL];
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) a[i] = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = s_m[w] == -INFINITY ? 0.f : expf(s_m[w] - M);
+            L = fmaf(s_l[w], f, L);
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) a[i] = fmaf(s_acc[w][lane * DPL + i], f, a[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) mine[2 + lane * DPL + i] = a[i];
+        if (lane == 0) {
+            mine[0] = M;
+            mine[1] = L;
+        }
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[h]);
+            last = cnt.fetch_add(1, cuda::memory_order_acq_rel) == n_split - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            cuda::atomic_thread_fence(cuda::memory_order_acquire, cuda::thread_scope_device);
+            const float* base = part + static_cast<int64_t>(h) * n_split * (head_dim + 2);
+            float MM = -INFINITY;
+            for (int s2 = 0; s2 < n_split; ++s2) MM = fmaxf(MM, base[s2 * (head_dim + 2)]);
+            float LL = 0.f, o[DPL];
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) o[i] = 0.f;
+            for (int s2 = 0; s2 < n_split; ++s2) {
+                const float* p = base + s2 * (head_dim + 2);
+                const float f = p[0] == -INFINITY ? 0.f : expf(p[0] - MM);
+                LL = fmaf(p[1], f, LL);
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) o[i] = fmaf(p[2 + lane * DPL + i], f, o[i]);
+            }
+            const float inv = 1.0f / LL;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) out[static_cast<int64_t>(h) * head_dim + lane * DPL + i] = o[i] * inv;
+            if (lane == 0) {
+                cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[h]);
+                cnt.store(0, cuda::memory_order_relaxed);
+            }
+        }
+    }
+}
+
+int grid_for(int64_t n, int threads, int cap = 148 * 8) {
+    int64_t g = (n + threads - 1) / threads;
+    if (g > cap) g = cap;
+    if (g < 1) g = 1;
+    return static_cast<int>(g);
+}
+
+}  // namespace
+
+cudaError_t matmul_f32(const float* a, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
+                       float* y, int64_t ldy, float scale, cudaStream_t s) {
+    matmul_f32_kernel<<<static_cast<int>((n_out + 7) / 8), 256, 0, s>>>(a, static_cast<int>(n_out),
+                                                                        static_cast<int>(k), x, ldx,
+                                                                        static_cast<int>(batch), y, ldy, scale);
+    return cudaGetLastError();
+}
+
+cudaError_t rms_norm(const float* in, const float* w, float* out, int64_t n_rows, int64_t n, float eps,
+                     cudaStream_t s) {
+    rms_norm_kernel<<<static_cast<int>(n_rows), 256, 0, s>>>(in, w, out, static_cast<int>(n), eps);
+    return cudaGetLastError();
+}
+
+cudaError_t silu_mul(const float* g, const float* u, float* o, int64_t n, cudaStream_t s) {
+    silu_mul_kernel<<<grid_for(n, 256), 256, 0, s>>>(g, u, o, n);
+    return cudaGetLastError();
+}
+
+cudaError_t binary(const float* a, const float* b, float* o, int64_t n, int op, cudaStream_t s) {
+    binary_kernel<<<grid_for(n, 256), 256, 0, s>>>(a, b, o, n, op);
+    return cudaGetLastError();
+}
+
+cudaError_t softmax(const float* in, float* out, int64_t n_rows, int64_t n, cudaStream_t s) {
+    softmax_kernel<<<static_cast<int>(n_rows), 256, 0, s>>>(in, out, static_cast<int>(n));
+    return cudaGetLastError();
+}
+
+cudaError_t rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, const int32_t* pos_dev,
+                 int32_t pos_host, cudaStream_t s) {
+    rope_kernel<<<grid_for(n_heads * head_dim / 2, 256, 64), 256, 0, s>>>(
+        data, static_cast<int>(n_heads), static_cast<int>(head_dim), table, pos_dev, pos_host);
+    return cudaGetLastError();
+}
+
+cudaError_t kv_store(const float* k, const float* v, void* kc, void* vc, int64_t row_elems, int64_t ctx,
+                     const int32_t* pos_dev, int32_t pos_host, cudaStream_t s) {
+    kv_store_kernel<<<grid_for(row_elems, 256, 64), 256, 0, s>>>(k, v, static_cast<__half*>(kc),
+                                                                  static_cast<__half*>(vc),
+                                                                  static_cast<int>(row_elems),
+                                                                  static_cast<int>(ctx), pos_dev, pos_host);
+    return cudaGetLastError();
+}
+
+size_t attention_workspace_bytes(int64_t n_head, int64_t head_dim, int64_t ctx) {
+    const int64_t n_split = attention_splits(ctx);
+    const size_t counters = ((static_cast<size_t>(n_head) * 4) + 255) & ~size_t(255);
+    return counters + static_cast<size_t>(n_head) * n_split * (head_dim + 2) * 4;
+}
+
+int attention_splits(int64_t ctx) {
+    // about 64 positions per warp-iteration group: 256 positions per CTA
+    int64_t n = (ctx + 255) / 256;
+    if (n < 1) n = 1;
+    if (n > 64) n = 64;
+    return static_cast<int>(n);
+}
+
+cudaError_t attention(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,
+                      int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
+                      void* workspace, cudaStream_t s) {
+    const int n_split = attention_splits(ctx);
+    const int chunk = static_cast<int>((ctx + n_split - 1) / n_split);
+    int* counters = static_cast<int*>(workspace);
+    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                           (((static_cast<size_t>(n_head) * 4) + 255) & ~size_t(255)));
+    dim3 grid(static_cast<unsigned>(n_head), static_cast<unsigned>(n_split));
+    const __half* k = static_cast<const __half*>(kc);
+    const __half* v = static_cast<const __half*>(vc);
+    const int nh = static_cast<int>(n_head), nkv = static_cast<int>(n_kv_head), c = static_cast<int>(ctx);
+    switch (head_dim) {
+        case 64: attention_kernel<2><<<grid, kAttnWarps * 32, 0, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
+        case 128: attention_kernel<4><<<grid, kAttnWarps * 32, 0, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
+        case 256: attention_kernel<8><<<grid, kAttnWarps * 32, 0, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace hesa_cuda

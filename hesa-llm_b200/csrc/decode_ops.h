@@ -1,0 +1,28 @@
+// decode_ops.h -- host launchers of the decode-step kernels (decode_ops.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace hesa_cuda {
+
+cudaError_t matmul_f32(const float* a, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
+                       float* y, int64_t ldy, float scale, cudaStream_t s);
+cudaError_t rms_norm(const float* in, const float* w, float* out, int64_t n_rows, int64_t n, float eps,
+                     cudaStream_t s);
+cudaError_t silu_mul(const float* g, const float* u, float* o, int64_t n, cudaStream_t s);
+cudaError_t binary(const float* a, const float* b, float* o, int64_t n, int op /*0 add, 1 mul*/,
+                   cudaStream_t s);
+cudaError_t softmax(const float* in, float* out, int64_t n_rows, int64_t n, cudaStream_t s);
+cudaError_t rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, const int32_t* pos_dev,
+                 int32_t pos_host, cudaStream_t s);
+cudaError_t kv_store(const float* k, const float* v, void* kc, void* vc, int64_t row_elems, int64_t ctx,
+                     const int32_t* pos_dev, int32_t pos_host, cudaStream_t s);
+int attention_splits(int64_t ctx);
+size_t attention_workspace_bytes(int64_t n_head, int64_t head_dim, int64_t ctx);
+cudaError_t attention(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,
+                      int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
+                      void* workspace, cudaStream_t s);
+
+}  // namespace hesa_cuda

@@ -36,6 +36,18 @@ SIGNATURES = [
     ("hesa_cuda_device_status", _int, [_vp, ctypes.POINTER(_int)]),
     ("hesa_cuda_clear_device_status", _int, [_vp]),
     ("hesa_cuda_last_error", ctypes.c_char_p, []),
+    ("hesa_cuda_matmul_f32", _int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _f, _vp]),
+    ("hesa_cuda_rms_norm", _int, [_vp, _vp, _vp, _i64, _i64, _f, _vp]),
+    ("hesa_cuda_silu_mul", _int, [_vp, _vp, _vp, _i64, _vp]),
+    ("hesa_cuda_add", _int, [_vp, _vp, _vp, _i64, _vp]),
+    ("hesa_cuda_mul", _int, [_vp, _vp, _vp, _i64, _vp]),
+    ("hesa_cuda_softmax", _int, [_vp, _vp, _i64, _i64, _vp]),
+    ("hesa_cuda_rope_table", _int, [_vp, ctypes.c_int32, _i64, _f]),
+    ("hesa_cuda_rope", _int, [_vp, _i64, _i64, _vp, _vp, ctypes.c_int32, _vp]),
+    ("hesa_cuda_kv_store", _int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, ctypes.c_int32, _vp]),
+    ("hesa_cuda_attention_workspace_size", _sz, [_i64, _i64, _i64]),
+    ("hesa_cuda_attention", _int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, ctypes.c_int32, _vp, _sz,
+                                   _vp]),
 ]
 
 
@@ -148,3 +160,99 @@ def loaded_library_files() -> list[str]:
     except OSError:
         pass
     return sorted(set(out))
+
+
+# --------------------------------------------------------------------------
+# decode-step helpers (device tensors in, device tensors out)
+# --------------------------------------------------------------------------
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def matmul_f32(a, x, y=None, scale: float = 1.0, stream=None):
+    import torch
+    x2 = x.unsqueeze(0) if x.dim() == 1 else x
+    batch, k = x2.shape
+    n_out = a.shape[0]
+    if y is None:
+        y = torch.empty((batch, n_out), dtype=torch.float32, device=x.device)
+    y2 = y.unsqueeze(0) if y.dim() == 1 else y
+    _check(lib().hesa_cuda_matmul_f32(a.data_ptr(), n_out, k, x2.data_ptr(), x2.stride(0), batch, y2.data_ptr(),
+                                      y2.stride(0), float(scale), _stream_handle(stream)))
+    return y2[0] if x.dim() == 1 else y2
+
+
+def rms_norm(x, w, eps: float = 1e-6, out=None, stream=None):
+    import torch
+    out = torch.empty_like(x) if out is None else out
+    n = x.shape[-1]
+    _check(lib().hesa_cuda_rms_norm(x.data_ptr(), w.data_ptr(), out.data_ptr(), x.numel() // n, n, float(eps),
+                                    _stream_handle(stream)))
+    return out
+
+
+def silu_mul(g, u=None, out=None, stream=None):
+    import torch
+    out = torch.empty_like(g) if out is None else out
+    _check(lib().hesa_cuda_silu_mul(g.data_ptr(), _ptr(u), out.data_ptr(), g.numel(), _stream_handle(stream)))
+    return out
+
+
+def add(a, b, out=None, stream=None):
+    import torch
+    out = torch.empty_like(a) if out is None else out
+    _check(lib().hesa_cuda_add(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), _stream_handle(stream)))
+    return out
+
+
+def mul(a, b, out=None, stream=None):
+    import torch
+    out = torch.empty_like(a) if out is None else out
+    _check(lib().hesa_cuda_mul(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), _stream_handle(stream)))
+    return out
+
+
+def softmax(x, out=None, stream=None):
+    import torch
+    out = torch.empty_like(x) if out is None else out
+    n = x.shape[-1]
+    _check(lib().hesa_cuda_softmax(x.data_ptr(), out.data_ptr(), x.numel() // n, n, _stream_handle(stream)))
+    return out
+
+
+def rope_table(n_pos: int, head_dim: int, base: float = 10000.0):
+    """Host-computed rotate-half angle table [n_pos, head_dim] (numpy)."""
+    import numpy as np
+    t = np.empty((n_pos, head_dim), dtype=np.float32)
+    _check(lib().hesa_cuda_rope_table(t.ctypes.data, n_pos, head_dim, float(base)))
+    return t
+
+
+def rope(x, n_heads: int, head_dim: int, table, pos=None, pos_dev=None, stream=None):
+    _check(lib().hesa_cuda_rope(x.data_ptr(), n_heads, head_dim, table.data_ptr(), _ptr(pos_dev),
+                                int(pos or 0), _stream_handle(stream)))
+    return x
+
+
+def kv_store(k, v, k_cache, v_cache, ctx: int, pos=None, pos_dev=None, stream=None):
+    _check(lib().hesa_cuda_kv_store(k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k.numel(),
+                                    ctx, _ptr(pos_dev), int(pos or 0), _stream_handle(stream)))
+
+
+def attention_workspace(n_head: int, head_dim: int, ctx: int, device=None):
+    import torch
+    nb = int(lib().hesa_cuda_attention_workspace_size(n_head, head_dim, ctx))
+    return torch.zeros(max(nb, 16), dtype=torch.uint8, device=device or "cuda")
+
+
+def attention(q, k_cache, v_cache, n_head: int, n_kv_head: int, head_dim: int, ctx: int, pos=None, pos_dev=None,
+              workspace=None, out=None, stream=None):
+    import torch
+    out = torch.empty_like(q) if out is None else out
+    if workspace is None:
+        workspace = attention_workspace(n_head, head_dim, ctx, device=q.device)
+    _check(lib().hesa_cuda_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), n_head,
+                                     n_kv_head, head_dim, ctx, _ptr(pos_dev), int(pos or 0), workspace.data_ptr(),
+                                     workspace.numel(), _stream_handle(stream)))
+    return out

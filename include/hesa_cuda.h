@@ -93,6 +93,72 @@ HESA_CUDA_API int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int
 HESA_CUDA_API int hesa_cuda_dequantize(int qtype, const void* w, int64_t n_rows, int64_t k,
                                        float* out, int64_t ldo, void* stream);
 
+/* ---------------------------------------------------------------------
+ * Decode-step helpers (single token). Semantics of hesa-llm's CPU kernels,
+ * src/backend/cpu_backend.cpp; `pos` arguments are a device int32 scalar
+ * (pos_dev, so a captured CUDA graph replays for every token) or, when
+ * pos_dev is NULL, the host value pos_host.
+ * --------------------------------------------------------------------- */
+
+/* y = scale * A @ x for row-major F32 A [n_out, k]: hesa::cpu_matmul_f32
+ * (src/backend/cpu_backend.cpp:24-41) for F32 weights, as
+ * Backend::matmul (include/hesa/backend.hpp:43-44) uses it. */
+HESA_CUDA_API int hesa_cuda_matmul_f32(const float* a, int64_t n_out, int64_t k, const float* x, int64_t ldx,
+                                       int64_t batch, float* y, int64_t ldy, float scale, void* stream);
+
+/* out = in * (1/sqrt(mean(in^2) + eps)) * weight per row of n:
+ * cpu_rms_norm_f32 (src/backend/cpu_backend.cpp:72-89), Backend::rms_norm
+ * (include/hesa/backend.hpp:48-49). */
+HESA_CUDA_API int hesa_cuda_rms_norm(const float* in, const float* weight, float* out, int64_t n_rows,
+                                     int64_t n, float eps, void* stream);
+
+/* out = silu(gate) * up, or silu(gate) when up is NULL: cpu_silu_f32
+ * (src/backend/cpu_backend.cpp:91-96), Backend::silu (backend.hpp:52). */
+HESA_CUDA_API int hesa_cuda_silu_mul(const float* gate, const float* up, float* out, int64_t n, void* stream);
+
+/* out = a + b, out = a * b: cpu_add_f32 (cpu_backend.cpp:43-46) and
+ * CPU_Backend::mul (cpu_backend.cpp:170-177); Backend::add/mul
+ * (backend.hpp:45-46). */
+HESA_CUDA_API int hesa_cuda_add(const float* a, const float* b, float* out, int64_t n, void* stream);
+HESA_CUDA_API int hesa_cuda_mul(const float* a, const float* b, float* out, int64_t n, void* stream);
+
+/* Row softmax over the last dimension: cpu_softmax_f32
+ * (cpu_backend.cpp:48-70), Backend::softmax (backend.hpp:47). */
+HESA_CUDA_API int hesa_cuda_softmax(const float* in, float* out, int64_t n_rows, int64_t n, void* stream);
+
+/* HOST function: the rotate-half angle table of cpu_rope_f32
+ * (cpu_backend.cpp:103-112), row p = [cos(theta_p,d) for d < head_dim/2,
+ * sin(theta_p,d) for d < head_dim/2] with theta = p / base^(2d/head_dim),
+ * for p in [0, n_pos). table_host holds n_pos * head_dim floats. */
+HESA_CUDA_API int hesa_cuda_rope_table(float* table_host, int32_t n_pos, int64_t head_dim, float freq_base);
+
+/* In-place rotate-half RoPE of data [n_heads, head_dim] at position pos,
+ * from a device copy of hesa_cuda_rope_table (cpu_rope_f32,
+ * cpu_backend.cpp:98-120; Backend::rope, backend.hpp:50-51). */
+HESA_CUDA_API int hesa_cuda_rope(float* data, int64_t n_heads, int64_t head_dim, const float* table,
+                                 const int32_t* pos_dev, int32_t pos_host, void* stream);
+
+/* Ring-buffer KV cache write: k_cache/v_cache [ctx, row_elems] fp16, slot
+ * pos % ctx <- fp16(k), fp16(v) (round to nearest even). The KV cache of
+ * the reference's design (docs/architecture.md:287-338). */
+HESA_CUDA_API int hesa_cuda_kv_store(const float* k, const float* v, void* k_cache, void* v_cache,
+                                     int64_t row_elems, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
+                                     void* stream);
+
+/* Workspace bytes of hesa_cuda_attention (zero-filled once; left zeroed). */
+HESA_CUDA_API size_t hesa_cuda_attention_workspace_size(int64_t n_head, int64_t head_dim, int64_t ctx);
+
+/* Single-query attention over min(pos+1, ctx) slots of the fp16 ring:
+ * out[h] = softmax(q[h] . K / sqrt(head_dim)) V with kv head
+ * h / (n_head / n_kv_head). q, out: [n_head, head_dim] fp32; head_dim 64,
+ * 128 or 256. The SDPA of CPU_Backend (cpu_backend.cpp:225-294) extended to
+ * GQA and the fp16 cache; Backend::scaled_dot_product_attention
+ * (backend.hpp:55-57). */
+HESA_CUDA_API int hesa_cuda_attention(const float* q, const void* k_cache, const void* v_cache, float* out,
+                                      int64_t n_head, int64_t n_kv_head, int64_t head_dim, int64_t ctx,
+                                      const int32_t* pos_dev, int32_t pos_host, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
 /* Sticky device-side status of the kernels' bounded waits: 0 when no wait
  * has ever timed out in this process, else a nonzero code naming the wait.
  * Reading synchronizes `stream`. hesa_cuda_clear_device_status resets it. */
