@@ -126,8 +126,9 @@ __global__ void rope_kernel(float* __restrict__ data, int n_heads, int head_dim,
         float* row = data + static_cast<int64_t>(h) * head_dim;
         const float c = cs[d], s = cs[half + d];
         const float x0 = row[d], x1 = row[d + half];
-        row[d] = x0 * c - x1 * s;
-        row[d + half] = x0 * s + x1 * c;
+        // separately rounded products and sums, as cpu_rope_f32 computes them
+        row[d] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        row[d + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
     }
 }
 

@@ -12,15 +12,22 @@
 //     private ring of shared-memory stages with cp.async.bulk; the ring runs
 //     up to kMaxStages steps ahead of the decode, so the copy engine keeps
 //     ~100 KB per SM in flight.
-//   * x is staged once per CTA in shared memory, permuted per type so that
-//     lane (unit j, quarter c) reads its 64 activations with 16 conflict-free
-//     128-bit loads, then keeps them in registers for all kRows rows.
-//   * Four lanes share a unit; lane c decodes a quarter (64 weights): the
-//     quant bits are moved into the top of an fp32 mantissa with one PRMT per
-//     weight (f = 0.5 + q * 2^-(bits+1), exact) and accumulated with packed
-//     fma.rn.f32x2, so sum_k q*x = 2^(bits+1)*S - 2^bits*X with X = sum_k x
-//     precomputed per quarter during staging. Scales are applied once per
-//     sub-block.
+//   * x is staged once per CTA in shared memory as exact integers: per unit
+//     of 256 activations, X = rint(x / s) with s a power of two chosen so
+//     |X| <= 2^22 (22 bits below the unit's largest magnitude), split into
+//     three balanced int8 digits X = 65536*D2 + 256*D1 + D0. The digit planes
+//     are permuted per type so lane (unit j, quarter c) reads its 64
+//     activations with 12 conflict-free 128-bit loads and keeps them in
+//     registers for all kRows rows.
+//   * Four lanes share a unit; lane c decodes a quarter (64 weights): quant
+//     values are unpacked to bytes with one or two LOP3/shifts per 4 weights
+//     and multiplied into the three digit planes with DP4A, an exact int32
+//     dot product. Sub-block scales are applied in int32 (sc * sum q*D), the
+//     q offsets (-8, -32) through per-group digit sums, and the three planes
+//     are combined in fp32 once per unit. The only rounding besides the final
+//     fp32 sums is the representation of x: relative L2 error of y below
+//     ~1e-6 for any activation distribution (each unit's error is bounded by
+//     2^-22 of its own largest |x|).
 //   * Row sums are reduced with warp shuffles. A row group split between
 //     warps is combined deterministically: every warp writes its partial to
 //     the workspace, and the last to arrive (acq_rel counter) adds the
@@ -42,7 +49,12 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRows = 4;           // rows per row group: x register reuse factor
 constexpr int kUnitsPerStep = 8;   // units per warp step (4 lanes per unit)
-constexpr int kXStride = 68;       // floats per (unit, quarter) in smem: 64 + 4 pad
+constexpr int kQPlaneStride = 208; // bytes per (unit, quarter): 3 digit planes x 64 B + 16 pad
+constexpr int kQSumStride = 80;    // bytes per (unit, quarter): 4 groups x int4 digit sums + 16 pad
+
+__host__ __device__ constexpr size_t x_region_bytes(int U) {
+    return static_cast<size_t>(U) * 4 * (kQPlaneStride + kQSumStride) + ((static_cast<size_t>(U) * 4 + 15) & ~size_t(15));
+}
 constexpr int kMaxStages = 4;
 constexpr int kMaxSmem = 227 * 1024;
 
@@ -60,7 +72,8 @@ __host__ __device__ constexpr int slot_bytes(int qt) {
 __host__ __device__ constexpr int stage_bytes(int qt) { return kRows * slot_bytes(qt); }
 
 // Slot (quarter c, index i) of activation P (0..255 inside a unit), in the
-// order the decoders consume it.
+// order the decoders consume it. Eight consecutive positions 8m..8m+7 always
+// land in one quarter at eight consecutive indices.
 template <int QT>
 __device__ __forceinline__ void unit_pos_to_slot(int P, int& c, int& i) {
     if constexpr (QT == kQ6_K) {
@@ -72,6 +85,10 @@ __device__ __forceinline__ void unit_pos_to_slot(int P, int& c, int& i) {
         i = P & 63;
     }
 }
+
+// Digit groups of a quarter: the weight blocks / sub-blocks whose integer
+// corrections need sum_k X_k (32 activations; 16 for Q6_K).
+template <int QT> __host__ __device__ constexpr int group_shift() { return QT == kQ6_K ? 4 : 5; }
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
@@ -86,130 +103,133 @@ __device__ __forceinline__ uint4 lds128_a2(const uint8_t* p) {
     return make_uint4(prmt(w0, w1, sel), prmt(w1, w2, sel), prmt(w2, w3, sel), prmt(w3, w4, sel));
 }
 
-// Bytes of t hold (q << (7 - bits)), bit 7 clear. Float i of the word is
-// 0.5 * (1 + q_i * 2^-bits): exponent byte 0x3F with the byte as the top
-// mantissa bits.
-__device__ __forceinline__ void acc_word(uint32_t t, const float* xv, float2& s) {
-    const float f0 = __uint_as_float(prmt(t, 0x3F000000u, 0x7044u));
-    const float f1 = __uint_as_float(prmt(t, 0x3F000000u, 0x7144u));
-    const float f2 = __uint_as_float(prmt(t, 0x3F000000u, 0x7244u));
-    const float f3 = __uint_as_float(prmt(t, 0x3F000000u, 0x7344u));
-    s = ffma2(make_float2(f0, f1), make_float2(xv[0], xv[1]), s);
-    s = ffma2(make_float2(f2, f3), make_float2(xv[2], xv[3]), s);
+// The activations of one (unit, quarter) as the decoders see them: X = x/s as
+// three balanced int8 digit planes, X = 65536*D2 + 256*D1 + D0, four digits
+// per word (word w of a plane = quarter indices 4w..4w+3), the per-group digit
+// sums, and the unit's scale s (a power of two).
+struct XQuarter {
+    uint32_t d[3][16];
+    int ds[4][3];
+    float s;
+};
+
+// Integer dot of 4 weight bytes (values that fit int8) with the 3 digit
+// planes at word w: p[j] += sum_i q_i * D_j,i.
+__device__ __forceinline__ void dot3(uint32_t q, const XQuarter& xq, int w, int (&p)[3]) {
+    p[0] = __dp4a(static_cast<int>(q), static_cast<int>(xq.d[0][w]), p[0]);
+    p[1] = __dp4a(static_cast<int>(q), static_cast<int>(xq.d[1][w]), p[1]);
+    p[2] = __dp4a(static_cast<int>(q), static_cast<int>(xq.d[2][w]), p[2]);
 }
 
-// Signed int8 bytes of w -> exact q, accumulated as sum q*x.
-__device__ __forceinline__ void acc_word_s8(uint32_t w, const float* xv, float2& s) {
-    const uint32_t u = w ^ 0x80808080u;  // biased: u = q + 128
-    const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    float2 a = make_float2(__uint_as_float(prmt(u, 0x4B000000u, 0x7440u)),
-                           __uint_as_float(prmt(u, 0x4B000000u, 0x7441u)));
-    float2 b = make_float2(__uint_as_float(prmt(u, 0x4B000000u, 0x7442u)),
-                           __uint_as_float(prmt(u, 0x4B000000u, 0x7443u)));
-    a = fadd2(a, bias);
-    b = fadd2(b, bias);
-    s = ffma2(a, make_float2(xv[0], xv[1]), s);
-    s = ffma2(b, make_float2(xv[2], xv[3]), s);
+// 65536*a2 + 256*a1 + a0 in fp32.
+__device__ __forceinline__ float combine3(int a0, int a1, int a2) {
+    return fmaf(static_cast<float>(a2), 65536.f, fmaf(static_cast<float>(a1), 256.f, static_cast<float>(a0)));
 }
 
-__device__ __forceinline__ float hsum(float2 v) { return v.x + v.y; }
+// sum_k x_k over group g of the quarter (fp32), from the digit sums.
+__device__ __forceinline__ float xsum(const XQuarter& xq, int g) {
+    return xq.s * combine3(xq.ds[g][0], xq.ds[g][1], xq.ds[g][2]);
+}
 
 // Contribution of quarter c of one unit of one row: sum over the quarter's
-// 64 weights of deq(w) * x. `u` points at the unit in shared memory, `xr` are
-// the quarter's activations in decode order and `xs` their partial sums.
+// 64 weights of deq(w) * x (without the row's output scale). `u` points at
+// the unit in shared memory.
 template <int QT>
-__device__ __forceinline__ float unit_dot(const uint8_t* u, int c, const float* xr, const float* xs);
+__device__ __forceinline__ float unit_dot(const uint8_t* u, int c, const XQuarter& xq);
+
+// K-quant scale/min pairs of sub-blocks 2c, 2c+1 (byte 0, byte 1 of each).
+__device__ __forceinline__ void kq_pairs(const uint4& h, int c, uint32_t& sc2, uint32_t& m2) {
+    const uint32_t s = 16u * (c & 1);
+    if (c >> 1) {
+        sc2 = ((h.w >> s) & 0x0F0Fu) | ((h.y >> (s + 2)) & 0x3030u);
+        m2 = ((h.w >> (s + 4)) & 0x0F0Fu) | ((h.z >> (s + 2)) & 0x3030u);
+    } else {
+        sc2 = (h.y >> s) & 0x3F3Fu;
+        m2 = (h.z >> s) & 0x3F3Fu;
+    }
+}
 
 template <>
-__device__ __forceinline__ float unit_dot<kQ4_K>(const uint8_t* u, int c, const float* xr, const float* xs) {
+__device__ __forceinline__ float unit_dot<kQ4_K>(const uint8_t* u, int c, const XQuarter& xq) {
     const uint4 h = lds128(u);
     const uint4 qa = lds128(u + 16 + 32 * c);
     const uint4 qb = lds128(u + 32 + 32 * c);
-    // scale / min pairs of sub-blocks 2c and 2c+1 (two bytes each)
-    const int hi = c >> 1;
-    const uint32_t s = 16u * (c & 1);
-    const uint32_t sc2 = hi ? (((h.w >> s) & 0x0F0Fu) | ((h.y >> (s + 2)) & 0x3030u)) : ((h.y >> s) & 0x3F3Fu);
-    const uint32_t m2 = hi ? (((h.w >> (s + 4)) & 0x0F0Fu) | ((h.z >> (s + 2)) & 0x3030u)) : ((h.z >> s) & 0x3F3Fu);
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
+    uint32_t sc2, m2;
+    kq_pairs(h, c, sc2, m2);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    int lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        acc_word((q[t] << 3) & 0x78787878u, xr + 4 * t, s0);
-        acc_word((q[t] >> 1) & 0x78787878u, xr + 32 + 4 * t, s1);
+        dot3(q[t] & 0x0F0F0F0Fu, xq, t, lo);          // sub-block 2c: indices 4t..4t+3
+        dot3((q[t] >> 4) & 0x0F0F0F0Fu, xq, 8 + t, hi);  // sub-block 2c+1: 32+4t..
     }
-    const float u0 = fmaf(32.f, hsum(s0), -16.f * xs[0]);
-    const float u1 = fmaf(32.f, hsum(s1), -16.f * xs[1]);
-    const float accd = fmaf(static_cast<float>(sc2 & 0xFF), u0, static_cast<float>(sc2 >> 8) * u1);
-    const float accm = fmaf(static_cast<float>(m2 & 0xFF), xs[0], static_cast<float>(m2 >> 8) * xs[1]);
-    return fmaf(d, accd, -dmin * accm);
+    const int s0 = static_cast<int>(sc2 & 0xFF), s1 = static_cast<int>(sc2 >> 8);
+    const float t = combine3(s0 * lo[0] + s1 * hi[0], s0 * lo[1] + s1 * hi[1], s0 * lo[2] + s1 * hi[2]);
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const float mins = fmaf(static_cast<float>(m2 & 0xFF), xsum(xq, 0), static_cast<float>(m2 >> 8) * xsum(xq, 1));
+    return fmaf(d * xq.s, t, -dmin * mins);
 }
 
 template <>
-__device__ __forceinline__ float unit_dot<kQ5_K>(const uint8_t* u, int c, const float* xr, const float* xs) {
+__device__ __forceinline__ float unit_dot<kQ5_K>(const uint8_t* u, int c, const XQuarter& xq) {
     const uint4 h = lds128(u);
     const uint4 ha = lds128(u + 16), hb = lds128(u + 32);   // qh, shared by the 4 quarters
     const uint4 qa = lds128(u + 48 + 32 * c);
     const uint4 qb = lds128(u + 64 + 32 * c);
-    const int hi = c >> 1;
-    const uint32_t s = 16u * (c & 1);
-    const uint32_t sc2 = hi ? (((h.w >> s) & 0x0F0Fu) | ((h.y >> (s + 2)) & 0x3030u)) : ((h.y >> s) & 0x3F3Fu);
-    const uint32_t m2 = hi ? (((h.w >> (s + 4)) & 0x0F0Fu) | ((h.z >> (s + 2)) & 0x3030u)) : ((h.z >> s) & 0x3F3Fu);
-    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
+    uint32_t sc2, m2;
+    kq_pairs(h, c, sc2, m2);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     const uint32_t qh[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
     const uint32_t sh = 2u * c;
+    int lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        const uint32_t hv = qh[t] >> sh;
-        // byte = q << 2 with q = nibble | (high bit << 4)
-        acc_word(((q[t] << 2) & 0x3C3C3C3Cu) | ((hv << 6) & 0x40404040u), xr + 4 * t, s0);
-        acc_word(((q[t] >> 2) & 0x3C3C3C3Cu) | ((hv << 5) & 0x40404040u), xr + 32 + 4 * t, s1);
+        const uint32_t hv = qh[t] >> sh;   // bit 0 of each byte: sub-block 2c, bit 1: 2c+1
+        dot3((q[t] & 0x0F0F0F0Fu) | ((hv << 4) & 0x10101010u), xq, t, lo);
+        dot3(((q[t] >> 4) & 0x0F0F0F0Fu) | ((hv << 3) & 0x10101010u), xq, 8 + t, hi);
     }
-    const float u0 = fmaf(64.f, hsum(s0), -32.f * xs[0]);
-    const float u1 = fmaf(64.f, hsum(s1), -32.f * xs[1]);
-    const float accd = fmaf(static_cast<float>(sc2 & 0xFF), u0, static_cast<float>(sc2 >> 8) * u1);
-    const float accm = fmaf(static_cast<float>(m2 & 0xFF), xs[0], static_cast<float>(m2 >> 8) * xs[1]);
-    return fmaf(d, accd, -dmin * accm);
+    const int s0 = static_cast<int>(sc2 & 0xFF), s1 = static_cast<int>(sc2 >> 8);
+    const float t = combine3(s0 * lo[0] + s1 * hi[0], s0 * lo[1] + s1 * hi[1], s0 * lo[2] + s1 * hi[2]);
+    const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    const float mins = fmaf(static_cast<float>(m2 & 0xFF), xsum(xq, 0), static_cast<float>(m2 >> 8) * xsum(xq, 1));
+    return fmaf(d * xq.s, t, -dmin * mins);
 }
 
 template <>
-__device__ __forceinline__ float unit_dot<kQ6_K>(const uint8_t* u, int c, const float* xr, const float* xs) {
+__device__ __forceinline__ float unit_dot<kQ6_K>(const uint8_t* u, int c, const XQuarter& xq) {
     // quarter c: half h = c>>1, positions l in [16*s2, 16*s2+16) of each of the
-    // four 32-weight groups of that half
+    // four 32-weight groups of that half; group g is sub-block 8h + s2 + 2g
     const int h = c >> 1, s2 = c & 1;
     const uint4 qa = lds128_a2(u + 64 * h + 16 * s2);
     const uint4 qb = lds128_a2(u + 64 * h + 32 + 16 * s2);
     const uint4 qv = lds128_a2(u + 128 + 32 * h + 16 * s2);
     const uint8_t* scp = u + 192 + 8 * h + s2;
-    const float sc0 = static_cast<float>(static_cast<int8_t>(scp[0]));
-    const float sc1 = static_cast<float>(static_cast<int8_t>(scp[2]));
-    const float sc2 = static_cast<float>(static_cast<int8_t>(scp[4]));
-    const float sc3 = static_cast<float>(static_cast<int8_t>(scp[6]));
-    const float d = h2f_bytes(u + 208);
-    float2 g0 = make_float2(0.f, 0.f), g1 = g0, g2 = g0, g3 = g0;
+    const int sc[4] = {static_cast<int8_t>(scp[0]), static_cast<int8_t>(scp[2]), static_cast<int8_t>(scp[4]),
+                       static_cast<int8_t>(scp[6])};
     const uint32_t a[4] = {qa.x, qa.y, qa.z, qa.w};
     const uint32_t b[4] = {qb.x, qb.y, qb.z, qb.w};
     const uint32_t v[4] = {qv.x, qv.y, qv.z, qv.w};
+    int g0[3] = {0, 0, 0}, g1[3] = {0, 0, 0}, g2[3] = {0, 0, 0}, g3[3] = {0, 0, 0};
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-        // byte = q << 1 with q = nibble | (two high bits << 4)
-        acc_word(((a[t] << 1) & 0x1E1E1E1Eu) | ((v[t] << 5) & 0x60606060u), xr + 4 * t, g0);
-        acc_word(((b[t] << 1) & 0x1E1E1E1Eu) | ((v[t] << 3) & 0x60606060u), xr + 16 + 4 * t, g1);
-        acc_word(((a[t] >> 3) & 0x1E1E1E1Eu) | ((v[t] << 1) & 0x60606060u), xr + 32 + 4 * t, g2);
-        acc_word(((b[t] >> 3) & 0x1E1E1E1Eu) | ((v[t] >> 1) & 0x60606060u), xr + 48 + 4 * t, g3);
+        // q = nibble | (two high bits << 4), 0..63
+        dot3((a[t] & 0x0F0F0F0Fu) | ((v[t] << 4) & 0x30303030u), xq, t, g0);
+        dot3((b[t] & 0x0F0F0F0Fu) | ((v[t] << 2) & 0x30303030u), xq, 4 + t, g1);
+        dot3(((a[t] >> 4) & 0x0F0F0F0Fu) | (v[t] & 0x30303030u), xq, 8 + t, g2);
+        dot3(((b[t] >> 4) & 0x0F0F0F0Fu) | ((v[t] >> 2) & 0x30303030u), xq, 12 + t, g3);
     }
-    // sum (q - 32) x = 128 S - 64 X - 32 X
-    float acc = sc0 * fmaf(128.f, hsum(g0), -96.f * xs[0]);
-    acc = fmaf(sc1, fmaf(128.f, hsum(g1), -96.f * xs[1]), acc);
-    acc = fmaf(sc2, fmaf(128.f, hsum(g2), -96.f * xs[2]), acc);
-    acc = fmaf(sc3, fmaf(128.f, hsum(g3), -96.f * xs[3]), acc);
-    return d * acc;
+    // sum (q - 32) X per group, scaled by the signed sub-block scale
+    int acc[3];
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+        acc[p] = sc[0] * (g0[p] - 32 * xq.ds[0][p]) + sc[1] * (g1[p] - 32 * xq.ds[1][p]) +
+                 sc[2] * (g2[p] - 32 * xq.ds[2][p]) + sc[3] * (g3[p] - 32 * xq.ds[3][p]);
+    const float d = h2f_bytes(u + 208);
+    return (d * xq.s) * combine3(acc[0], acc[1], acc[2]);
 }
 
 template <>
-__device__ __forceinline__ float unit_dot<kQ4_0>(const uint8_t* u, int c, const float* xr, const float* xs) {
+__device__ __forceinline__ float unit_dot<kQ4_0>(const uint8_t* u, int c, const XQuarter& xq) {
     // quarter c = blocks 2c and 2c+1: 36 bytes at 36c (4-byte aligned)
     const uint8_t* p = u + 36 * c;
     uint32_t w[9];
@@ -220,21 +240,23 @@ __device__ __forceinline__ float unit_dot<kQ4_0>(const uint8_t* u, int c, const 
     const uint32_t q0[4] = {prmt(w[0], w[1], 0x5432u), prmt(w[1], w[2], 0x5432u),
                             prmt(w[2], w[3], 0x5432u), prmt(w[3], w[4], 0x5432u)};
     const uint32_t q1[4] = {w[5], w[6], w[7], w[8]};
-    float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+    int b0[3] = {0, 0, 0}, b1[3] = {0, 0, 0};
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         // byte j low nibble -> weight j, high nibble -> weight j + 16
-        acc_word((q0[t] << 3) & 0x78787878u, xr + 4 * t, s0);
-        acc_word((q0[t] >> 1) & 0x78787878u, xr + 16 + 4 * t, s0);
-        acc_word((q1[t] << 3) & 0x78787878u, xr + 32 + 4 * t, s1);
-        acc_word((q1[t] >> 1) & 0x78787878u, xr + 48 + 4 * t, s1);
+        dot3(q0[t] & 0x0F0F0F0Fu, xq, t, b0);
+        dot3((q0[t] >> 4) & 0x0F0F0F0Fu, xq, 4 + t, b0);
+        dot3(q1[t] & 0x0F0F0F0Fu, xq, 8 + t, b1);
+        dot3((q1[t] >> 4) & 0x0F0F0F0Fu, xq, 12 + t, b1);
     }
-    // sum (q - 8) x = 32 S - 16 X - 8 X
-    return fmaf(d0, fmaf(32.f, hsum(s0), -24.f * xs[0]), d1 * fmaf(32.f, hsum(s1), -24.f * xs[1]));
+    // sum (q - 8) X
+    const float t0 = combine3(b0[0] - 8 * xq.ds[0][0], b0[1] - 8 * xq.ds[0][1], b0[2] - 8 * xq.ds[0][2]);
+    const float t1 = combine3(b1[0] - 8 * xq.ds[1][0], b1[1] - 8 * xq.ds[1][1], b1[2] - 8 * xq.ds[1][2]);
+    return xq.s * fmaf(d0, t0, d1 * t1);
 }
 
 template <>
-__device__ __forceinline__ float unit_dot<kQ8_0>(const uint8_t* u, int c, const float* xr, const float*) {
+__device__ __forceinline__ float unit_dot<kQ8_0>(const uint8_t* u, int c, const XQuarter& xq) {
     // quarter c = blocks 2c and 2c+1: 68 bytes at 68c (4-byte aligned)
     const uint8_t* p = u + 68 * c;
     uint32_t w[17];
@@ -242,13 +264,13 @@ __device__ __forceinline__ float unit_dot<kQ8_0>(const uint8_t* u, int c, const 
     for (int i = 0; i < 17; ++i) w[i] = lds32(p + 4 * i);
     const float d0 = half_bits_to_float(w[0]);
     const float d1 = half_bits_to_float(w[8] >> 16);
-    float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+    int b0[3] = {0, 0, 0}, b1[3] = {0, 0, 0};
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        acc_word_s8(prmt(w[t], w[t + 1], 0x5432u), xr + 4 * t, s0);
-        acc_word_s8(w[9 + t], xr + 32 + 4 * t, s1);
+        dot3(prmt(w[t], w[t + 1], 0x5432u), xq, t, b0);
+        dot3(w[9 + t], xq, 8 + t, b1);
     }
-    return fmaf(d0, hsum(s0), d1 * hsum(s1));
+    return xq.s * fmaf(d0, combine3(b0[0], b0[1], b0[2]), d1 * combine3(b1[0], b1[1], b1[2]));
 }
 
 struct StepPlan {
@@ -297,10 +319,12 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
     const size_t total_bytes = pitch * static_cast<size_t>(n_out);
     const size_t total_floor16 = total_bytes & ~size_t(15);
 
-    // shared memory: [x: U*4*kXStride f32][xsum: U*4*4 f32][stages][mbarriers]
-    float* xs_smem = reinterpret_cast<float*>(smem);
-    float* xsum_smem = xs_smem + static_cast<size_t>(U) * 4 * kXStride;
-    uint8_t* stage_base = reinterpret_cast<uint8_t*>(xsum_smem + static_cast<size_t>(U) * 16);
+    // shared memory: [x digit planes: U*4*kQPlaneStride][digit sums: U*4*kQSumStride]
+    //                [unit scales: U f32][stages][mbarriers]
+    uint8_t* xplanes = smem;
+    uint8_t* xsums = xplanes + static_cast<size_t>(U) * 4 * kQPlaneStride;
+    float* xscale = reinterpret_cast<float*>(xsums + static_cast<size_t>(U) * 4 * kQSumStride);
+    uint8_t* stage_base = smem + x_region_bytes(U);
     uint8_t* my_stages = stage_base + static_cast<size_t>(warp) * n_stages * STAGE;
     uint64_t* bars = reinterpret_cast<uint64_t*>(stage_base + static_cast<size_t>(kWarps) * n_stages * STAGE) +
                      warp * kMaxStages;
@@ -354,24 +378,65 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
         }
     }
 
-    // ---- stage x (permuted, padded) and the per-quarter partial sums ----
-    for (int p0 = warp * 32; p0 < k; p0 += kThreads) {
-        const int p = p0 + lane;
-        const float v = x[p];
-        const int unit = p >> 8;
-        int c, i;
-        unit_pos_to_slot<QT>(p & 255, c, i);
-        xs_smem[(unit * 4 + c) * kXStride + i] = v;
-        float sum = v;
-        if constexpr (QT == kQ6_K) {
+    // ---- stage x: per unit of 256 activations, X = rint(x / s) with s a power
+    // of two chosen so |X| <= 2^22, split into three balanced int8 digits
+    // (X = 65536*D2 + 256*D1 + D0) stored as permuted digit planes, plus the
+    // per-group digit sums the bias corrections use. One warp per unit; lane L
+    // holds positions 8L..8L+7.
+    for (int unit = warp; unit < U; unit += kWarps) {
+        const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(unit) * 256 + lane * 8);
+        const float4 va = xp[0], vb = xp[1];
+        const float v[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+        float am = 0.f;
+        bool nonfinite = false;
 #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if ((lane & 15) == 0) xsum_smem[(unit * 4 + c) * 4 + (i >> 4)] = sum;
-        } else {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) xsum_smem[(unit * 4 + c) * 4 + (i >> 5)] = sum;
+        for (int j = 0; j < 8; ++j) {
+            am = fmaxf(am, fabsf(v[j]));
+            nonfinite |= !(fabsf(v[j]) <= 3.402823466e38f);  // inf or NaN
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        // a non-finite activation makes the unit's scale NaN, so every output
+        // it touches is NaN, as the fp32 reference sum would be inf or NaN
+        const bool finite = !__any_sync(0xffffffffu, nonfinite);
+        // exponent E of the largest magnitude: |x| < 2^(E+1); s = 2^(E-21)
+        int E = static_cast<int>((__float_as_uint(am) >> 23) & 0xFFu) - 127;
+        if (E < -100) E = -100;  // activations below 2^-100 round to zero
+        const float inv_s = __uint_as_float(static_cast<uint32_t>(21 - E + 127) << 23);
+        const float s = finite ? __uint_as_float(static_cast<uint32_t>(E - 21 + 127) << 23) : __int_as_float(0x7FC00000);
+        uint32_t dw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int X = finite ? __float2int_rn(v[j] * inv_s) : 0;
+            const int d0 = (X << 24) >> 24;
+            const int X1 = (X - d0) >> 8;
+            const int d1 = (X1 << 24) >> 24;
+            const int d2 = (X1 - d1) >> 8;
+            const int sh = 8 * (j & 3);
+            dw[0][j >> 2] |= (static_cast<uint32_t>(d0) & 0xFFu) << sh;
+            dw[1][j >> 2] |= (static_cast<uint32_t>(d1) & 0xFFu) << sh;
+            dw[2][j >> 2] |= (static_cast<uint32_t>(d2) & 0xFFu) << sh;
+        }
+        int c, i0;
+        unit_pos_to_slot<QT>(lane * 8, c, i0);
+        uint8_t* qbase = xplanes + static_cast<size_t>(unit * 4 + c) * kQPlaneStride;
+#pragma unroll
+        for (int p = 0; p < 3; ++p)
+            *reinterpret_cast<uint2*>(qbase + p * 64 + i0) = make_uint2(dw[p][0], dw[p][1]);
+        int sums[3];
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+            sums[p] = __dp4a(static_cast<int>(dw[p][0]), 0x01010101, __dp4a(static_cast<int>(dw[p][1]), 0x01010101, 0));
+            sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 1);
+            if constexpr (QT != kQ6_K) sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 2);
+        }
+        const bool writer = (QT == kQ6_K) ? ((lane & 1) == 0) : ((lane & 3) == 0);
+        if (writer) {
+            int* ds = reinterpret_cast<int*>(xsums + static_cast<size_t>(unit * 4 + c) * kQSumStride) +
+                      4 * (i0 >> group_shift<QT>());
+            *reinterpret_cast<int4*>(ds) = make_int4(sums[0], sums[1], sums[2], 0);
+        }
+        if (lane == 0) xscale[unit] = s;
     }
     __syncthreads();
 
@@ -398,22 +463,32 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
         const uint8_t* st = my_stages + stage * STAGE;
         if (ju < sp.n) {
             const int unit = sp.u0 + ju;
-            float xr[64];
-            const float4* xsrc = reinterpret_cast<const float4*>(xs_smem + (unit * 4 + qc) * kXStride);
+            // this lane's activations, kept in registers for the kRows rows
+            XQuarter xq;
+            const uint8_t* qsrc = xplanes + static_cast<size_t>(unit * 4 + qc) * kQPlaneStride;
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
-                const float4 v = xsrc[t];
-                xr[4 * t] = v.x; xr[4 * t + 1] = v.y; xr[4 * t + 2] = v.z; xr[4 * t + 3] = v.w;
+            for (int p = 0; p < 3; ++p) {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const uint4 w4 = lds128(qsrc + p * 64 + 16 * t);
+                    xq.d[p][4 * t] = w4.x; xq.d[p][4 * t + 1] = w4.y;
+                    xq.d[p][4 * t + 2] = w4.z; xq.d[p][4 * t + 3] = w4.w;
+                }
             }
-            const float4 xsv = *reinterpret_cast<const float4*>(xsum_smem + (unit * 4 + qc) * 4);
-            const float xsum[4] = {xsv.x, xsv.y, xsv.z, xsv.w};
+            const uint8_t* ssrc = xsums + static_cast<size_t>(unit * 4 + qc) * kQSumStride;
+#pragma unroll
+            for (int g = 0; g < (QT == kQ6_K ? 4 : 2); ++g) {
+                const int4 s4 = *reinterpret_cast<const int4*>(ssrc + 16 * g);
+                xq.ds[g][0] = s4.x; xq.ds[g][1] = s4.y; xq.ds[g][2] = s4.z;
+            }
+            xq.s = xscale[unit];
 #pragma unroll
             for (int r = 0; r < kRows; ++r) {
                 const int row = sp.g * kRows + r;
                 if (row < n_out) {
                     const size_t start = static_cast<size_t>(row) * pitch + static_cast<size_t>(sp.u0) * UB;
                     const uint8_t* up = st + r * SLOT + (start & 15) + ju * UB;
-                    acc[r] += unit_dot<QT>(up, qc, xr, xsum);
+                    acc[r] += unit_dot<QT>(up, qc, xq);
                 }
             }
         }
@@ -564,7 +639,7 @@ template <int QT>
 cudaError_t launch_stream(const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
                           int* counters, float* partials, int grid, cudaStream_t stream) {
     const int U = k >> 8;
-    const size_t x_bytes = static_cast<size_t>(U) * 4 * kXStride * 4 + static_cast<size_t>(U) * 16 * 4;
+    const size_t x_bytes = x_region_bytes(U);
     const size_t per_stage = static_cast<size_t>(kWarps) * stage_bytes(QT);
     const size_t bar_bytes = static_cast<size_t>(kWarps) * kMaxStages * 8;
     if (x_bytes + per_stage + bar_bytes > static_cast<size_t>(kMaxSmem)) return cudaErrorInvalidValue;
