@@ -62,7 +62,7 @@ int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int64_t k, const 
         return fail(HESA_CUDA_INVALID_ARGUMENT, "x / y must be 16-byte aligned with ldx, ldy multiples of 4");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    if (hesa_cuda::qmv_stream_eligible(w, n_out, k)) {
+    if (hesa_cuda::qmv_stream_eligible(qtype, w, n_out, k)) {
         const size_t need = hesa_cuda::qmv_workspace_bytes(static_cast<int>(n_out));
         if (!workspace || workspace_bytes < need) return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace too small");
         if (!aligned16(workspace)) return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace must be 16-byte aligned");

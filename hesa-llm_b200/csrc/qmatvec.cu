@@ -2,13 +2,13 @@
 // plus the exact dequantizer and a generic per-row kernel for odd shapes.
 //
 // Streaming kernel (qmv_stream_kernel):
-//   * Work is a grid of cells: (row group of kRows rows) x (unit of 256 weights
+//   * Work is a grid of cells: (row group of 4 rows; 2 for Q8_0) x (unit of 256 weights
 //     = one K-quant super-block or eight 32-weight blocks). Every warp of the
 //     persistent grid owns a contiguous, equal-sized range of cells in
 //     row-group-major order, so HBM traffic is balanced to +-1 cell per warp
 //     whatever n_out and k are.
 //   * A warp step covers up to 8 consecutive units of one row group. Lane 0
-//     copies the step's kRows row segments (contiguous bytes of W) into a
+//     copies the step's row segments (contiguous bytes of W) into a
 //     private ring of shared-memory stages with cp.async.bulk; the ring runs
 //     up to kMaxStages steps ahead of the decode, so the copy engine keeps
 //     ~100 KB per SM in flight.
@@ -18,7 +18,7 @@
 //     three balanced int8 digits X = 65536*D2 + 256*D1 + D0. The digit planes
 //     are permuted per type so lane (unit j, quarter c) reads its 64
 //     activations with 12 conflict-free 128-bit loads and keeps them in
-//     registers for all kRows rows.
+//     registers for all rows of the group.
 //   * Four lanes share a unit; lane c decodes a quarter (64 weights): quant
 //     values are unpacked to bytes with one or two LOP3/shifts per 4 weights
 //     and multiplied into the three digit planes with DP4A, an exact int32
@@ -45,9 +45,9 @@ __device__ int g_hesa_status = 0;
 
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 12;          // 384 threads: up to 168 registers each
 constexpr int kThreads = kWarps * 32;
-constexpr int kRows = 4;           // rows per row group: x register reuse factor
+constexpr int kMaxRows = 4;        // rows per row group (x register reuse factor), Q8_0: 2
 constexpr int kUnitsPerStep = 8;   // units per warp step (4 lanes per unit)
 constexpr int kQPlaneStride = 208; // bytes per (unit, quarter): 3 digit planes x 64 B + 16 pad
 constexpr int kQSumStride = 80;    // bytes per (unit, quarter): 4 groups x int4 digit sums + 16 pad
@@ -69,7 +69,9 @@ __host__ __device__ constexpr int slot_bytes(int qt) {
     return ((kUnitsPerStep * unit_bytes(qt) + 15) / 16) * 16 + 32;
 }
 
-__host__ __device__ constexpr int stage_bytes(int qt) { return kRows * slot_bytes(qt); }
+__host__ __device__ constexpr int rows_of(int qt) { return qt == kQ8_0 ? 2 : kMaxRows; }
+
+__host__ __device__ constexpr int stage_bytes(int qt) { return rows_of(qt) * slot_bytes(qt); }
 
 // Slot (quarter c, index i) of activation P (0..255 inside a unit), in the
 // order the decoders consume it. Eight consecutive positions 8m..8m+7 always
@@ -273,22 +275,29 @@ __device__ __forceinline__ float unit_dot<kQ8_0>(const uint8_t* u, int c, const 
     return xq.s * fmaf(d0, combine3(b0[0], b0[1], b0[2]), d1 * combine3(b1[0], b1[1], b1[2]));
 }
 
-struct StepPlan {
-    int g;       // row group
-    int u0;      // first unit
-    int n;       // units in the step (1..8)
+// Division-free walk over a warp's cells in row-group-major order: a step
+// covers up to kUnitsPerStep units of one row group.
+struct Cursor {
+    int64_t c;  // next cell
+    int g;      // its row group
+    int u;      // its unit within the row group
 };
 
-__device__ __forceinline__ StepPlan plan_step(int64_t c, int64_t c_end, int units_per_row) {
-    StepPlan s;
-    s.g = static_cast<int>(c / units_per_row);
-    s.u0 = static_cast<int>(c - static_cast<int64_t>(s.g) * units_per_row);
-    const int64_t left = c_end - c;
-    int n = units_per_row - s.u0;
+__device__ __forceinline__ int step_units(const Cursor& cur, int64_t c_end, int U) {
+    int n = U - cur.u;
     if (n > kUnitsPerStep) n = kUnitsPerStep;
+    const int64_t left = c_end - cur.c;
     if (left < n) n = static_cast<int>(left);
-    s.n = n;
-    return s;
+    return n;
+}
+
+__device__ __forceinline__ void advance(Cursor& cur, int n, int U) {
+    cur.c += n;
+    cur.u += n;
+    if (cur.u == U) {
+        cur.u = 0;
+        ++cur.g;
+    }
 }
 
 // Warp that owns cell c when C cells are split over W warps as [wC/W, (w+1)C/W).
@@ -297,11 +306,68 @@ __device__ __forceinline__ int64_t owner_warp(int64_t c, int64_t C, int64_t W) {
     return ((c + 1) * W - 1) / C;
 }
 
+// Convert one unit (256 activations) to digit planes in shared memory; lane
+// L holds positions 8L..8L+7 in v.
+template <int QT>
+__device__ __forceinline__ void stage_unit(int unit, int lane, const float (&v)[8], uint8_t* xplanes, uint8_t* xsums,
+                                           float* xscale) {
+    float am = 0.f;
+    bool nonfinite = false;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        am = fmaxf(am, fabsf(v[j]));
+        nonfinite |= !(fabsf(v[j]) <= 3.402823466e38f);  // inf or NaN
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    // a non-finite activation makes the unit's scale NaN, so every output it
+    // touches is NaN, as the fp32 reference sum would be inf or NaN
+    const bool finite = !__any_sync(0xffffffffu, nonfinite);
+    // exponent E of the largest magnitude: |x| < 2^(E+1); s = 2^(E-21)
+    int E = static_cast<int>((__float_as_uint(am) >> 23) & 0xFFu) - 127;
+    if (E < -100) E = -100;  // activations below 2^-100 round to zero
+    const float inv_s = __uint_as_float(static_cast<uint32_t>(21 - E + 127) << 23);
+    const float s = finite ? __uint_as_float(static_cast<uint32_t>(E - 21 + 127) << 23) : __int_as_float(0x7FC00000);
+    uint32_t dw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int X = finite ? __float2int_rn(v[j] * inv_s) : 0;
+        const int d0 = (X << 24) >> 24;
+        const int X1 = (X - d0) >> 8;
+        const int d1 = (X1 << 24) >> 24;
+        const int d2 = (X1 - d1) >> 8;
+        const int sh = 8 * (j & 3);
+        dw[0][j >> 2] |= (static_cast<uint32_t>(d0) & 0xFFu) << sh;
+        dw[1][j >> 2] |= (static_cast<uint32_t>(d1) & 0xFFu) << sh;
+        dw[2][j >> 2] |= (static_cast<uint32_t>(d2) & 0xFFu) << sh;
+    }
+    int c, i0;
+    unit_pos_to_slot<QT>(lane * 8, c, i0);
+    uint8_t* qbase = xplanes + static_cast<size_t>(unit * 4 + c) * kQPlaneStride;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) *reinterpret_cast<uint2*>(qbase + p * 64 + i0) = make_uint2(dw[p][0], dw[p][1]);
+    int sums[3];
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        sums[p] = __dp4a(static_cast<int>(dw[p][0]), 0x01010101, __dp4a(static_cast<int>(dw[p][1]), 0x01010101, 0));
+        sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 1);
+        if constexpr (QT != kQ6_K) sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 2);
+    }
+    const bool writer = (QT == kQ6_K) ? ((lane & 1) == 0) : ((lane & 3) == 0);
+    if (writer) {
+        int* ds = reinterpret_cast<int*>(xsums + static_cast<size_t>(unit * 4 + c) * kQSumStride) +
+                  4 * (i0 >> group_shift<QT>());
+        *reinterpret_cast<int4*>(ds) = make_int4(sums[0], sums[1], sums[2], 0);
+    }
+    if (lane == 0) xscale[unit] = s;
+}
+
 template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
 qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
                   float* __restrict__ y, float scale, int* __restrict__ counters,
                   float* __restrict__ partials, int n_stages, int* __restrict__ status) {
+    constexpr int R = rows_of(QT);
     constexpr int UB = unit_bytes(QT);
     constexpr int SLOT = slot_bytes(QT);
     constexpr int STAGE = stage_bytes(QT);
@@ -310,7 +376,7 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int U = k >> 8;                                     // units per row
-    const int G = (n_out + kRows - 1) / kRows;               // row groups
+    const int G = (n_out + R - 1) / R;                        // row groups
     const int64_t C = static_cast<int64_t>(G) * U;           // cells
     const int64_t W = static_cast<int64_t>(gridDim.x) * kWarps;
     const int64_t gw = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
@@ -335,20 +401,25 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
     }
     __syncwarp();
 
-    // ---- producer (lane 0): copy the kRows row segments of one step ----
-    auto issue = [&](const StepPlan& sp, int stage) {
+    Cursor first;
+    first.c = c_begin;
+    first.g = static_cast<int>(c_begin / U);
+    first.u = static_cast<int>(c_begin - static_cast<int64_t>(first.g) * U);
+
+    // ---- producer (lane 0): copy the R row segments of one step ----
+    auto issue = [&](const Cursor& cur, int n, int stage) {
         uint8_t* dst = my_stages + stage * STAGE;
         uint32_t tx = 0;
-        const uint8_t* srcs[kRows];
-        uint32_t lens[kRows];
+        const uint8_t* srcs[R];
+        uint32_t lens[R];
+        const size_t base = static_cast<size_t>(cur.g) * R * pitch + static_cast<size_t>(cur.u) * UB;
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
+        for (int r = 0; r < R; ++r) {
             lens[r] = 0;
             srcs[r] = nullptr;
-            const int row = sp.g * kRows + r;
-            if (row >= n_out) continue;
-            const size_t start = static_cast<size_t>(row) * pitch + static_cast<size_t>(sp.u0) * UB;
-            const size_t end = start + static_cast<size_t>(sp.n) * UB;
+            if (cur.g * R + r >= n_out) continue;
+            const size_t start = base + r * pitch;
+            const size_t end = start + static_cast<size_t>(n) * UB;
             const size_t a0 = start & ~size_t(15);
             size_t a1 = (end + 15) & ~size_t(15);
             if (a1 > total_floor16) {
@@ -362,18 +433,18 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
         }
         mbar_arrive_expect_tx(&bars[stage], tx);
 #pragma unroll
-        for (int r = 0; r < kRows; ++r)
+        for (int r = 0; r < R; ++r)
             if (lens[r]) bulk_g2s(dst + r * SLOT, srcs[r], lens[r], &bars[stage]);
     };
 
     // Prime the ring before staging x so the copies overlap the staging.
-    int64_t prod_c = c_begin;
+    Cursor prod = first;
     int prod_step = 0;
     if (lane == 0) {
-        while (prod_step < n_stages && prod_c < c_end) {
-            const StepPlan sp = plan_step(prod_c, c_end, U);
-            issue(sp, prod_step);
-            prod_c += sp.n;
+        while (prod_step < n_stages && prod.c < c_end) {
+            const int n = step_units(prod, c_end, U);
+            issue(prod, n, prod_step);
+            advance(prod, n, U);
             ++prod_step;
         }
     }
@@ -381,77 +452,42 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
     // ---- stage x: per unit of 256 activations, X = rint(x / s) with s a power
     // of two chosen so |X| <= 2^22, split into three balanced int8 digits
     // (X = 65536*D2 + 256*D1 + D0) stored as permuted digit planes, plus the
-    // per-group digit sums the bias corrections use. One warp per unit; lane L
-    // holds positions 8L..8L+7.
-    for (int unit = warp; unit < U; unit += kWarps) {
-        const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(unit) * 256 + lane * 8);
-        const float4 va = xp[0], vb = xp[1];
-        const float v[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
-        float am = 0.f;
-        bool nonfinite = false;
+    // per-group digit sums the bias corrections use. One warp per unit; the
+    // loads of a batch of units are issued together.
+    constexpr int kBatch = 4;
+    for (int ub = warp; ub < U; ub += kWarps * kBatch) {
+        float v[kBatch][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            am = fmaxf(am, fabsf(v[j]));
-            nonfinite |= !(fabsf(v[j]) <= 3.402823466e38f);  // inf or NaN
+        for (int j = 0; j < kBatch; ++j) {
+            const int unit = ub + j * kWarps;
+            if (unit < U) {
+                const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(unit) * 256 + lane * 8);
+                const float4 va = xp[0], vb = xp[1];
+                v[j][0] = va.x; v[j][1] = va.y; v[j][2] = va.z; v[j][3] = va.w;
+                v[j][4] = vb.x; v[j][5] = vb.y; v[j][6] = vb.z; v[j][7] = vb.w;
+            }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-        // a non-finite activation makes the unit's scale NaN, so every output
-        // it touches is NaN, as the fp32 reference sum would be inf or NaN
-        const bool finite = !__any_sync(0xffffffffu, nonfinite);
-        // exponent E of the largest magnitude: |x| < 2^(E+1); s = 2^(E-21)
-        int E = static_cast<int>((__float_as_uint(am) >> 23) & 0xFFu) - 127;
-        if (E < -100) E = -100;  // activations below 2^-100 round to zero
-        const float inv_s = __uint_as_float(static_cast<uint32_t>(21 - E + 127) << 23);
-        const float s = finite ? __uint_as_float(static_cast<uint32_t>(E - 21 + 127) << 23) : __int_as_float(0x7FC00000);
-        uint32_t dw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int X = finite ? __float2int_rn(v[j] * inv_s) : 0;
-            const int d0 = (X << 24) >> 24;
-            const int X1 = (X - d0) >> 8;
-            const int d1 = (X1 << 24) >> 24;
-            const int d2 = (X1 - d1) >> 8;
-            const int sh = 8 * (j & 3);
-            dw[0][j >> 2] |= (static_cast<uint32_t>(d0) & 0xFFu) << sh;
-            dw[1][j >> 2] |= (static_cast<uint32_t>(d1) & 0xFFu) << sh;
-            dw[2][j >> 2] |= (static_cast<uint32_t>(d2) & 0xFFu) << sh;
+        for (int j = 0; j < kBatch; ++j) {
+            const int unit = ub + j * kWarps;
+            if (unit < U) stage_unit<QT>(unit, lane, v[j], xplanes, xsums, xscale);
         }
-        int c, i0;
-        unit_pos_to_slot<QT>(lane * 8, c, i0);
-        uint8_t* qbase = xplanes + static_cast<size_t>(unit * 4 + c) * kQPlaneStride;
-#pragma unroll
-        for (int p = 0; p < 3; ++p)
-            *reinterpret_cast<uint2*>(qbase + p * 64 + i0) = make_uint2(dw[p][0], dw[p][1]);
-        int sums[3];
-#pragma unroll
-        for (int p = 0; p < 3; ++p) {
-            sums[p] = __dp4a(static_cast<int>(dw[p][0]), 0x01010101, __dp4a(static_cast<int>(dw[p][1]), 0x01010101, 0));
-            sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 1);
-            if constexpr (QT != kQ6_K) sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 2);
-        }
-        const bool writer = (QT == kQ6_K) ? ((lane & 1) == 0) : ((lane & 3) == 0);
-        if (writer) {
-            int* ds = reinterpret_cast<int*>(xsums + static_cast<size_t>(unit * 4 + c) * kQSumStride) +
-                      4 * (i0 >> group_shift<QT>());
-            *reinterpret_cast<int4*>(ds) = make_int4(sums[0], sums[1], sums[2], 0);
-        }
-        if (lane == 0) xscale[unit] = s;
     }
     __syncthreads();
 
     // ---- consumer: all lanes ----
     const int ju = lane >> 2;   // unit within the step
     const int qc = lane & 3;    // quarter within the unit
-    float acc[kRows];
+    float acc[R];
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
 
     bool failed = false;
-    int64_t cons_c = c_begin;
+    Cursor cons = first;
     int cons_step = 0;
-    while (cons_c < c_end) {
-        const StepPlan sp = plan_step(cons_c, c_end, U);
+    while (cons.c < c_end) {
+        const int n = step_units(cons, c_end, U);
+        const int g = cons.g, u0 = cons.u;
         const int stage = cons_step % n_stages;
         const uint32_t parity = static_cast<uint32_t>(cons_step / n_stages) & 1u;
         // every lane waits; the warp leaves together if any lane gave up
@@ -461,9 +497,9 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
             break;
         }
         const uint8_t* st = my_stages + stage * STAGE;
-        if (ju < sp.n) {
-            const int unit = sp.u0 + ju;
-            // this lane's activations, kept in registers for the kRows rows
+        if (ju < n) {
+            const int unit = u0 + ju;
+            // this lane's activations, kept in registers for the R rows
             XQuarter xq;
             const uint8_t* qsrc = xplanes + static_cast<size_t>(unit * 4 + qc) * kQPlaneStride;
 #pragma unroll
@@ -477,76 +513,75 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
             }
             const uint8_t* ssrc = xsums + static_cast<size_t>(unit * 4 + qc) * kQSumStride;
 #pragma unroll
-            for (int g = 0; g < (QT == kQ6_K ? 4 : 2); ++g) {
-                const int4 s4 = *reinterpret_cast<const int4*>(ssrc + 16 * g);
-                xq.ds[g][0] = s4.x; xq.ds[g][1] = s4.y; xq.ds[g][2] = s4.z;
+            for (int gg = 0; gg < (QT == kQ6_K ? 4 : 2); ++gg) {
+                const int4 s4 = *reinterpret_cast<const int4*>(ssrc + 16 * gg);
+                xq.ds[gg][0] = s4.x; xq.ds[gg][1] = s4.y; xq.ds[gg][2] = s4.z;
             }
             xq.s = xscale[unit];
+            const size_t base = static_cast<size_t>(g) * R * pitch + static_cast<size_t>(u0) * UB;
 #pragma unroll
-            for (int r = 0; r < kRows; ++r) {
-                const int row = sp.g * kRows + r;
-                if (row < n_out) {
-                    const size_t start = static_cast<size_t>(row) * pitch + static_cast<size_t>(sp.u0) * UB;
+            for (int r = 0; r < R; ++r) {
+                if (g * R + r < n_out) {
+                    const size_t start = base + r * pitch;
                     const uint8_t* up = st + r * SLOT + (start & 15) + ju * UB;
                     acc[r] += unit_dot<QT>(up, qc, xq);
                 }
             }
         }
         __syncwarp();
-        cons_c += sp.n;
+        advance(cons, n, U);
         ++cons_step;
 
         // refill this stage with the step n_stages ahead
-        if (lane == 0 && prod_c < c_end) {
+        if (lane == 0 && prod.c < c_end) {
             fence_proxy_async_smem();
-            const StepPlan np = plan_step(prod_c, c_end, U);
-            issue(np, stage);
-            prod_c += np.n;
+            const int n2 = step_units(prod, c_end, U);
+            issue(prod, n2, stage);
+            advance(prod, n2, U);
             ++prod_step;
         }
 
-        // flush the row group when the next step leaves it (or the range ends)
-        const bool group_done = (cons_c >= c_end) || (cons_c / U != sp.g);
-        if (group_done) {
+        // flush the row group when the walk leaves it (or the range ends)
+        if (cons.c >= c_end || cons.u == 0) {
 #pragma unroll
-            for (int r = 0; r < kRows; ++r) {
+            for (int r = 0; r < R; ++r) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
             }
-            const int64_t g_first = static_cast<int64_t>(sp.g) * U;
+            const int64_t g_first = static_cast<int64_t>(g) * U;
             const int64_t g_last = g_first + U;   // exclusive
             if (lane == 0) {
                 if (g_first >= c_begin && g_last <= c_end) {
 #pragma unroll
-                    for (int r = 0; r < kRows; ++r) {
-                        const int row = sp.g * kRows + r;
+                    for (int r = 0; r < R; ++r) {
+                        const int row = g * R + r;
                         if (row < n_out) y[row] = acc[r] * scale;
                     }
                 } else {
                     // split group: partial -> workspace, last arrival sums in warp order
                     const int slot = (g_first <= c_begin) ? 0 : 1;   // head group : tail group
-                    float* mine = partials + (gw * 2 + slot) * kRows;
+                    float* mine = partials + (gw * 2 + slot) * kMaxRows;
 #pragma unroll
-                    for (int r = 0; r < kRows; ++r) mine[r] = acc[r];
+                    for (int r = 0; r < R; ++r) mine[r] = acc[r];
                     const int64_t w_first = owner_warp(g_first, C, W);
                     const int64_t w_last = owner_warp(g_last - 1, C, W);
                     const int n_parts = static_cast<int>(w_last - w_first + 1);
-                    cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[sp.g]);
+                    cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[g]);
                     const int prev = cnt.fetch_add(1, cuda::memory_order_acq_rel);
                     if (prev == n_parts - 1) {
-                        float tot[kRows];
+                        float tot[R];
 #pragma unroll
-                        for (int r = 0; r < kRows; ++r) tot[r] = 0.f;
+                        for (int r = 0; r < R; ++r) tot[r] = 0.f;
                         for (int64_t ow = w_first; ow <= w_last; ++ow) {
                             const int64_t oc0 = ow * C / W;
-                            const int oslot = (ow == w_first && oc0 / U != sp.g) ? 1 : 0;
-                            const float* pp = partials + (ow * 2 + oslot) * kRows;
+                            const int oslot = (ow == w_first && oc0 / U != g) ? 1 : 0;
+                            const float* pp = partials + (ow * 2 + oslot) * kMaxRows;
 #pragma unroll
-                            for (int r = 0; r < kRows; ++r) tot[r] += pp[r];
+                            for (int r = 0; r < R; ++r) tot[r] += pp[r];
                         }
 #pragma unroll
-                        for (int r = 0; r < kRows; ++r) {
-                            const int row = sp.g * kRows + r;
+                        for (int r = 0; r < R; ++r) {
+                            const int row = g * R + r;
                             if (row < n_out) y[row] = tot[r] * scale;
                         }
                         cnt.store(0, cuda::memory_order_relaxed);
@@ -554,7 +589,7 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
                 }
             }
 #pragma unroll
-            for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+            for (int r = 0; r < R; ++r) acc[r] = 0.f;
         }
     }
 
@@ -692,22 +727,27 @@ cudaError_t launch_dequant(const uint8_t* w, int64_t n_rows, int64_t k, float* o
 // ---------------------------------------------------------------------------
 
 size_t qmv_workspace_bytes(int n_out) {
-    const size_t groups = (static_cast<size_t>(n_out) + kRows - 1) / kRows;
+    // counters for the largest number of row groups (2-row groups of Q8_0)
+    const size_t groups = (static_cast<size_t>(n_out) + 1) / 2;
     const size_t counters = ((groups * sizeof(int)) + 255) & ~size_t(255);
-    const size_t partials = static_cast<size_t>(kMaxGridCtas) * kWarps * 2 * kRows * sizeof(float);
+    const size_t partials = static_cast<size_t>(kMaxGridCtas) * kWarps * 2 * kMaxRows * sizeof(float);
     return counters + partials;
 }
 
-bool qmv_stream_eligible(const void* w, int64_t n_out, int64_t k) {
-    const int64_t cells = ((n_out + kRows - 1) / kRows) * (k / 256);
-    // every warp of the grid must own at least one cell (the split-group
-    // combine counts every warp between the first and the last owner)
-    return (k % 256 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0) && cells >= kWarps &&
-           k <= 32768 && n_out < (int64_t(1) << 30);
+static int64_t stream_cells(int qtype, int64_t n_out, int64_t k) {
+    const int R = rows_of(qtype);
+    return ((n_out + R - 1) / R) * (k / 256);
 }
 
-int qmv_stream_grid(int64_t n_out, int64_t k) {
-    const int64_t cells = ((n_out + kRows - 1) / kRows) * (k / 256);
+bool qmv_stream_eligible(int qtype, const void* w, int64_t n_out, int64_t k) {
+    // every warp of the grid must own at least one cell (the split-group
+    // combine counts every warp between the first and the last owner)
+    return (k % 256 == 0) && (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+           stream_cells(qtype, n_out, k) >= kWarps && k <= 32768 && n_out < (int64_t(1) << 30);
+}
+
+int qmv_stream_grid(int qtype, int64_t n_out, int64_t k) {
+    const int64_t cells = stream_cells(qtype, n_out, k);
     // at least ~4 cells per warp so the per-step overhead amortises, and never
     // more warps than cells
     int64_t grid = device_sms();
@@ -721,12 +761,14 @@ int qmv_stream_grid(int64_t n_out, int64_t k) {
 
 cudaError_t qmv_stream(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
                        float scale, void* workspace, cudaStream_t stream, int grid_override) {
-    const size_t groups = (static_cast<size_t>(n_out) + kRows - 1) / kRows;
+    if (!qtype_supported(qtype)) return cudaErrorInvalidValue;
+    const int R = rows_of(qtype);
+    const size_t groups = (static_cast<size_t>(n_out) + R - 1) / R;
     int* counters = static_cast<int*>(workspace);
     float* partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
                                                (((groups * sizeof(int)) + 255) & ~size_t(255)));
-    int grid = grid_override > 0 ? grid_override : qmv_stream_grid(n_out, k);
-    const int64_t cells = static_cast<int64_t>(groups) * (k / 256);
+    int grid = grid_override > 0 ? grid_override : qmv_stream_grid(qtype, n_out, k);
+    const int64_t cells = stream_cells(qtype, n_out, k);
     if (static_cast<int64_t>(grid) * kWarps > cells) grid = static_cast<int>(cells / kWarps);
     if (grid < 1 || grid > kMaxGridCtas) return cudaErrorInvalidValue;
     const uint8_t* wb = static_cast<const uint8_t*>(w);

@@ -12,8 +12,8 @@ namespace hesa_cuda {
 constexpr int kMaxGridCtas = 1024;
 
 size_t qmv_workspace_bytes(int n_out);
-bool qmv_stream_eligible(const void* w, int64_t n_out, int64_t k);
-int qmv_stream_grid(int64_t n_out, int64_t k);
+bool qmv_stream_eligible(int qtype, const void* w, int64_t n_out, int64_t k);
+int qmv_stream_grid(int qtype, int64_t n_out, int64_t k);
 
 // Batch-1 streaming matvec on CUDA cores. workspace: qmv_workspace_bytes(n_out)
 // bytes, zero-filled before first use (left zero-filled on success).
