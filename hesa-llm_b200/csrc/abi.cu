@@ -222,3 +222,39 @@ int hesa_cuda_attention(const float* q, const void* k_cache, const void* v_cache
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// allocation-free matvec
+// ---------------------------------------------------------------------------
+
+extern "C" int hesa_cuda_qmatvec_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x,
+                                         int64_t ldx, int64_t batch, float* y, int64_t ldy, float scale,
+                                         void* stream) {
+    if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
+    if (!w || !x || !y) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_out <= 0 || k <= 0 || batch <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "non-positive dimension");
+    if (n_out > hesa_cuda::qmv_noalloc_max_rows())
+        return fail(HESA_CUDA_SHAPE_MISMATCH,
+                    "n_out exceeds the 65536 rows the library's fixed scratch array covers; "
+                    "use hesa_cuda_qmatvec with a caller workspace");
+    if (k >= (int64_t(1) << 31)) return fail(HESA_CUDA_SHAPE_MISMATCH, "dimension too large");
+    if (k % hesa_cuda::block_elems(qtype) != 0)
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "k is not a multiple of the block size");
+    if (ldx < k || (batch > 1 && ldy < n_out)) return fail(HESA_CUDA_SHAPE_MISMATCH, "leading dimension too small");
+    if (!aligned16(w)) return fail(HESA_CUDA_INVALID_ARGUMENT, "weights must be 16-byte aligned");
+    if (!aligned16(x) || !aligned16(y) || (ldx & 3) || (batch > 1 && (ldy & 3)))
+        return fail(HESA_CUDA_INVALID_ARGUMENT, "x / y must be 16-byte aligned with ldx, ldy multiples of 4");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (hesa_cuda::qmv_stream_eligible(qtype, w, n_out, k)) {
+        for (int64_t b = 0; b < batch; ++b) {
+            e = hesa_cuda::qmv_stream_noalloc(qtype, w, n_out, k, x + b * ldx, y + b * ldy, scale, s);
+            if (e != cudaSuccess) return cuda_fail(e, "qmatvec no-alloc stream kernel");
+        }
+    } else {
+        // the row-wise kernel needs no scratch
+        e = hesa_cuda::qmv_rowwise(qtype, w, n_out, k, x, ldx, batch, y, ldy, scale, s);
+        if (e != cudaSuccess) return cuda_fail(e, "qmatvec rowwise kernel");
+    }
+    return HESA_CUDA_OK;
+}

@@ -797,6 +797,70 @@ cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, cons
     }
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the batch-1 streaming matvec.
+//
+// The streaming kernel needs scratch for the row groups that straddle two
+// warps (arrival counters and partial sums). hesa_cuda_qmatvec takes it from
+// the caller; this variant keeps it in the fixed array below instead, for
+// callers that may not allocate device memory at all. The array lives in
+// every GPU that loads the library until the process exits.
+//   counters: kNoAllocGroups ints   (row groups of 2 rows -> n_out <= 65536)
+//   partials: kMaxGridCtas * kWarps * 2 * kMaxRows floats
+// In host code `g_noalloc_scratch` only names the symbol; its device address
+// comes from cudaGetSymbolAddress, looked up once per device with that device
+// current, on the first call there.
+// ---------------------------------------------------------------------------
+
+constexpr size_t kNoAllocGroups = 32768;
+constexpr size_t kNoAllocCounterBytes = kNoAllocGroups * sizeof(int);
+constexpr size_t kNoAllocPartialBytes = static_cast<size_t>(kMaxGridCtas) * kWarps * 2 * kMaxRows * sizeof(float);
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocPartialBytes;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+static uint8_t* g_noalloc_ptr[64] = {nullptr};
+
+int64_t qmv_noalloc_max_rows() { return static_cast<int64_t>(kNoAllocGroups) * 2; }
+
+cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
+                               float scale, cudaStream_t stream) {
+    if (!qtype_supported(qtype) || n_out > qmv_noalloc_max_rows()) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+    }
+    uint8_t* scratch = g_noalloc_ptr[dev];
+    // the counters must start at zero; the array keeps whatever the last call
+    // (possibly a failed one) left there
+    const int R = rows_of(qtype);
+    const size_t groups = (static_cast<size_t>(n_out) + R - 1) / R;
+    e = cudaMemsetAsync(scratch, 0, groups * sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+    int* counters = reinterpret_cast<int*>(scratch);
+    float* partials = reinterpret_cast<float*>(scratch + kNoAllocCounterBytes);
+    int grid = qmv_stream_grid(qtype, n_out, k);
+    const int64_t cells = stream_cells(qtype, n_out, k);
+    if (static_cast<int64_t>(grid) * kWarps > cells) grid = static_cast<int>(cells / kWarps);
+    if (grid < 1 || grid > kMaxGridCtas) return cudaErrorInvalidValue;
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const int n = static_cast<int>(n_out), kk = static_cast<int>(k);
+    switch (qtype) {
+        case kQ4_0: return launch_stream<kQ4_0>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ8_0: return launch_stream<kQ8_0>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ4_K: return launch_stream<kQ4_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ5_K: return launch_stream<kQ5_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        case kQ6_K: return launch_stream<kQ6_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t read_device_status(int* out) {
     return cudaMemcpyFromSymbol(out, g_hesa_status, sizeof(int));
 }

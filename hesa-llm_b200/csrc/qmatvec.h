@@ -20,6 +20,12 @@ int qmv_stream_grid(int qtype, int64_t n_out, int64_t k);
 cudaError_t qmv_stream(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
                        float scale, void* workspace, cudaStream_t stream, int grid_override);
 
+// Same kernel with its scratch in a fixed device array owned by the library
+// (no caller workspace, no allocation). Rows limited to qmv_noalloc_max_rows().
+int64_t qmv_noalloc_max_rows();
+cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
+                               float scale, cudaStream_t stream);
+
 // One warp per row, any k that is a multiple of the block size.
 cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,
                         int64_t batch, float* y, int64_t ldy, float scale, cudaStream_t stream);

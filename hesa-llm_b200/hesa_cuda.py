@@ -32,6 +32,7 @@ SIGNATURES = [
     ("hesa_cuda_row_bytes", _sz, [_int, _i64]),
     ("hesa_cuda_qmatvec_workspace_size", _sz, [_int, _i64, _i64, _i64]),
     ("hesa_cuda_qmatvec", _int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _f, _vp, _sz, _vp]),
+    ("hesa_cuda_qmatvec_noalloc", _int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _f, _vp]),
     ("hesa_cuda_dequantize", _int, [_int, _vp, _i64, _i64, _vp, _i64, _vp]),
     ("hesa_cuda_device_status", _int, [_vp, ctypes.POINTER(_int)]),
     ("hesa_cuda_clear_device_status", _int, [_vp]),

@@ -84,6 +84,27 @@ HESA_CUDA_API int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int
                                     float* y, int64_t ldy, float scale,
                                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* hesa_cuda_qmatvec without a workspace argument, for callers that cannot
+ * allocate device memory: code embedded in a host program that owns every
+ * device allocation through its own pool or budget (a stray cudaMalloc would
+ * break that accounting), or a serving loop that must not allocate after
+ * start-up. Same arguments, semantics and results as hesa_cuda_qmatvec; it
+ * has no counterpart in the reference.
+ *   - The kernel's scratch (arrival counters and cross-warp partial sums) is
+ *     a fixed 512 KB array inside this library, held on every GPU that loads
+ *     it until the process exits. n_out is limited to 65536 rows; larger
+ *     n_out is rejected with HESA_CUDA_SHAPE_MISMATCH and a message.
+ *   - Nothing is allocated: no cudaMalloc, cudaFree or allocating library
+ *     call. The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - Every call shares the array and clears the part that must start at
+ *     zero, so calls that overlap on the GPU (different streams, or several
+ *     host threads) race and give wrong results: serialize them. */
+HESA_CUDA_API int hesa_cuda_qmatvec_noalloc(int qtype, const void* w, int64_t n_out, int64_t k,
+                                            const float* x, int64_t ldx, int64_t batch,
+                                            float* y, int64_t ldy, float scale, void* stream);
+
 /* out[r*ldo + i] = deq(W[r, i]) for r < n_rows, i < k: the exact fp32 value
  * of every weight, bit-identical to the GGUF definition ((d*sc)*q - dmin*m
  * with each operation rounded separately). Used for embedding-row lookups
