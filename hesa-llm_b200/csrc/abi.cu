@@ -62,7 +62,13 @@ int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int64_t k, const 
         return fail(HESA_CUDA_INVALID_ARGUMENT, "x / y must be 16-byte aligned with ldx, ldy multiples of 4");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    if (hesa_cuda::qmv_stream_eligible(qtype, w, n_out, k)) {
+    if (hesa_cuda::qmv_strip_eligible(qtype, w, n_out, k)) {
+        // row strips: no workspace needed
+        for (int64_t b = 0; b < batch; ++b) {
+            e = hesa_cuda::qmv_strip(qtype, w, n_out, k, x + b * ldx, y + b * ldy, scale, s);
+            if (e != cudaSuccess) return cuda_fail(e, "qmatvec strip kernel");
+        }
+    } else if (hesa_cuda::qmv_stream_eligible(qtype, w, n_out, k)) {
         const size_t need = hesa_cuda::qmv_workspace_bytes(static_cast<int>(n_out));
         if (!workspace || workspace_bytes < need) return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace too small");
         if (!aligned16(workspace)) return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace must be 16-byte aligned");

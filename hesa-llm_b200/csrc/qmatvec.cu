@@ -603,6 +603,226 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
     }
 }
 
+// ---------------------------------------------------------------------------
+// Row-strip kernel (qmv_strip_kernel): the batch-1 path for k <= 24576.
+//
+//   * CTA b owns the contiguous rows [b*n_out/G, (b+1)*n_out/G) (balanced to
+//     one row). Its bytes are one contiguous range of W, streamed as chunks of
+//     chunk_rows whole rows, one cp.async.bulk per chunk, into a ring of up to
+//     kStripMaxSlots shared-memory slots; for decode-size matrices the whole
+//     range is in flight from the first microsecond.
+//   * Lane (slice s, quarter-column q) owns 64 weights of every row r with
+//     r = s (mod slices): unit q/4, quarter q%4. It builds that quarter of x as
+//     digit planes once, straight from global memory, and keeps it in
+//     registers for all its rows. Whole warps belong to one slice.
+//   * Per row, a warp's lanes are reduced with shuffles and lane 0 stores
+//     the warp's partial in shared memory; at the end the CTA adds the warps'
+//     partials of each row in a fixed order. No workspace, deterministic.
+//   * A chunk's slot is refilled by the last warp to finish it (shared
+//     counter), so no thread waits on the producer side.
+// ---------------------------------------------------------------------------
+
+constexpr int kStripMaxSlots = 16;
+
+// Sum of v[0..3] over the 32 lanes of a warp in 6 shuffles: afterwards the
+// lanes with (lane & 7) == 0 hold the total of v[reduce4_row(lane)].
+__device__ __forceinline__ int reduce4_row(int lane) { return ((lane >> 3) & 2) | ((lane >> 3) & 1); }
+
+__device__ __forceinline__ float reduce4(const float (&v)[4], int lane) {
+    const bool hi16 = lane & 16;
+    float a0 = hi16 ? v[2] : v[0], a1 = hi16 ? v[3] : v[1];
+    const float b0 = hi16 ? v[0] : v[2], b1 = hi16 ? v[1] : v[3];
+    a0 += __shfl_xor_sync(0xffffffffu, b0, 16);
+    a1 += __shfl_xor_sync(0xffffffffu, b1, 16);
+    const bool hi8 = lane & 8;
+    float c = hi8 ? a1 : a0;
+    const float d = hi8 ? a0 : a1;
+    c += __shfl_xor_sync(0xffffffffu, d, 8);
+    c += __shfl_xor_sync(0xffffffffu, c, 4);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    return c;
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kThreads, 1)
+qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
+                 float* __restrict__ y, float scale, int chunk_rows, int n_slots, int slot_stride, int rows_cap,
+                 int* __restrict__ status) {
+    constexpr int UB = unit_bytes(QT);
+    extern __shared__ __align__(128) uint8_t smem[];
+
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int U = k >> 8;
+    const int QC = 4 * U;                      // quarter-columns
+    const int wps = (QC + 31) >> 5;            // warps per row slice
+    const int RS = kWarps / wps;               // row slices (host: wps <= kWarps)
+    const int active_warps = RS * wps;
+    const int slice = warp / wps;
+    const int wq = warp - slice * wps;         // warp index inside its slice
+    const int q = wq * 32 + lane;
+    const bool wactive = slice < RS;
+    const bool qactive = wactive && q < QC;
+    const int unit = q >> 2, qc = q & 3;
+    const int r0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_out / gridDim.x);
+    const int r1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_out / gridDim.x);
+    const int nrows = r1 - r0;
+    const size_t pitch = static_cast<size_t>(U) * UB;
+    const size_t total_floor16 = (pitch * static_cast<size_t>(n_out)) & ~size_t(15);
+    const int CR = chunk_rows;                 // multiple of RS
+    const int n_chunks = (nrows + CR - 1) / CR;
+
+    // shared memory: [x digit planes, sums, scales (x_region_bytes)][slots]
+    //                [partials: rows_cap x wps f32][full mbarriers][done counters][issued]
+    uint8_t* xplanes = smem;
+    uint8_t* xsums = xplanes + static_cast<size_t>(U) * 4 * kQPlaneStride;
+    float* xscale = reinterpret_cast<float*>(xsums + static_cast<size_t>(U) * 4 * kQSumStride);
+    uint8_t* slots = smem + x_region_bytes(U);
+    float* part = reinterpret_cast<float*>(slots + static_cast<size_t>(n_slots) * slot_stride);
+    uint64_t* full = reinterpret_cast<uint64_t*>(
+        reinterpret_cast<uint8_t*>(part) + ((static_cast<size_t>(rows_cap) * wps * 4 + 15) & ~size_t(15)));
+    int* done = reinterpret_cast<int*>(full + kStripMaxSlots);
+    int* issued = done + kStripMaxSlots;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < n_slots; ++s) {
+            mbar_init(&full[s], 1);
+            done[s] = 0;
+            issued[s] = -1;
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // copy chunk j (rows [j*CR, j*CR + CR) of this CTA) into its slot
+    auto issue = [&](int j) {
+        const int slot = j % n_slots;
+        const int lr0 = j * CR;
+        const int lr1 = min(nrows, lr0 + CR);
+        const size_t start = static_cast<size_t>(r0 + lr0) * pitch;
+        const size_t end = static_cast<size_t>(r0 + lr1) * pitch;
+        const size_t a0 = start & ~size_t(15);
+        size_t a1 = (end + 15) & ~size_t(15);
+        uint8_t* dst = slots + static_cast<size_t>(slot) * slot_stride;
+        if (a1 > total_floor16) {
+            // the last < 16 bytes of W: plain loads, never past the buffer
+            a1 = total_floor16 > a0 ? total_floor16 : a0;
+            for (size_t b = a1; b < end; ++b) dst[b - a0] = w[b];
+        }
+        issued[slot] = j;
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(a1 - a0));
+        if (a1 > a0) bulk_g2s(dst, w + a0, static_cast<uint32_t>(a1 - a0), &full[slot]);
+    };
+
+    if (threadIdx.x == 0)
+        for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
+
+    // x as digit planes, converted once per CTA (one warp per unit of 256;
+    // the loads of a batch of units are issued together)
+    constexpr int kBatch = 4;
+    for (int ub = warp; ub < U; ub += kWarps * kBatch) {
+        float v[kBatch][8];
+#pragma unroll
+        for (int jb = 0; jb < kBatch; ++jb) {
+            const int u = ub + jb * kWarps;
+            if (u < U) {
+                const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(u) * 256 + lane * 8);
+                const float4 va = xp[0], vb = xp[1];
+                v[jb][0] = va.x; v[jb][1] = va.y; v[jb][2] = va.z; v[jb][3] = va.w;
+                v[jb][4] = vb.x; v[jb][5] = vb.y; v[jb][6] = vb.z; v[jb][7] = vb.w;
+            }
+        }
+#pragma unroll
+        for (int jb = 0; jb < kBatch; ++jb) {
+            const int u = ub + jb * kWarps;
+            if (u < U) stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
+        }
+    }
+    __syncthreads();
+
+    // this lane's quarter of x, in registers for every row it processes
+    XQuarter xq;
+    if (qactive) {
+        const uint8_t* qsrc = xplanes + static_cast<size_t>(unit * 4 + qc) * kQPlaneStride;
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const uint4 w4 = lds128(qsrc + p * 64 + 16 * t);
+                xq.d[p][4 * t] = w4.x; xq.d[p][4 * t + 1] = w4.y;
+                xq.d[p][4 * t + 2] = w4.z; xq.d[p][4 * t + 3] = w4.w;
+            }
+        }
+        const uint8_t* ssrc = xsums + static_cast<size_t>(unit * 4 + qc) * kQSumStride;
+#pragma unroll
+        for (int gg = 0; gg < (QT == kQ6_K ? 4 : 2); ++gg) {
+            const int4 s4 = *reinterpret_cast<const int4*>(ssrc + 16 * gg);
+            xq.ds[gg][0] = s4.x; xq.ds[gg][1] = s4.y; xq.ds[gg][2] = s4.z;
+        }
+        xq.s = xscale[unit];
+    }
+
+    bool failed = false;
+    if (wactive) {
+        for (int j = 0; j < n_chunks; ++j) {
+            const int slot = j % n_slots;
+            const uint32_t parity = static_cast<uint32_t>(j / n_slots) & 1u;
+            const bool landed = mbar_wait_bounded(&full[slot], parity, status, kStatusWaitTimeout);
+            if (!__all_sync(0xffffffffu, landed)) {
+                failed = true;
+                break;
+            }
+            const int lr0 = j * CR;
+            const int lr1 = min(nrows, lr0 + CR);
+            const uint8_t* base = slots + static_cast<size_t>(slot) * slot_stride +
+                                  ((static_cast<size_t>(r0 + lr0) * pitch) & 15) + static_cast<size_t>(unit) * UB;
+            // this slice's rows of the chunk, four at a time: independent
+            // decode chains, then one transposing reduction for the four
+            for (int i0 = lr0 + slice; i0 < lr1; i0 += 4 * RS) {
+                float a[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int i = i0 + t * RS;
+                    a[t] = (qactive && i < lr1) ? unit_dot<QT>(base + static_cast<size_t>(i - lr0) * pitch, qc, xq) : 0.f;
+                }
+                const int row = i0 + RS * reduce4_row(lane);
+                const float tot = reduce4(a, lane);
+                if ((lane & 7) == 0 && row < lr1) part[row * wps + wq] = tot;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                // the last warp out of the chunk refills its slot
+                if (atomicAdd(&done[slot], 1) == active_warps - 1) {
+                    done[slot] = 0;
+                    if (j + n_slots < n_chunks) {
+                        fence_proxy_async_smem();
+                        issue(j + n_slots);
+                    }
+                }
+            }
+        }
+    }
+    failed = __syncthreads_or(failed);
+    if (failed) {
+        // drain: wait (bounded) for the copy last issued into every slot
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < n_slots; ++s) {
+                const int j = issued[s];
+                if (j >= 0 && !mbar_wait_bounded(&full[s], static_cast<uint32_t>(j / n_slots) & 1u, status,
+                                                 kStatusDrainTimeout))
+                    break;
+            }
+        }
+        return;
+    }
+    for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
+        float s = 0.f;
+        for (int t = 0; t < wps; ++t) s += part[i * wps + t];
+        y[r0 + i] = s * scale;
+    }
+}
+
 // Generic kernel for shapes the streaming kernel does not take (k not a
 // multiple of 256, W not 16-byte aligned, tiny matrices): one warp per row,
 // exact per-weight decode from global memory, fp32 FMA, shuffle reduction.
@@ -700,6 +920,76 @@ cudaError_t launch_stream(const uint8_t* w, int n_out, int k, const float* x, fl
     return cudaGetLastError();
 }
 
+struct StripPlan {
+    int grid = 0, chunk_rows = 0, n_slots = 0, slot_stride = 0, rows_cap = 0;
+    size_t smem = 0;
+};
+
+// Launch geometry of the row-strip kernel: one CTA per SM (at most one per
+// row), chunks of a multiple of the row-slice count near 24 KB, and as many
+// ring slots as shared memory holds (no more than the CTA has chunks).
+bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
+    if (!qtype_supported(qt) || k % 256 != 0 || n_out < 1) return false;
+    const int U = static_cast<int>(k >> 8);
+    const int wps = (4 * U + 31) / 32;
+    if (wps > kWarps) return false;
+    const int RS = kWarps / wps;
+    const size_t pitch = static_cast<size_t>(U) * unit_bytes(qt);
+    int64_t grid = device_sms();
+    if (grid > n_out) grid = n_out;
+    p.grid = static_cast<int>(grid);
+    p.rows_cap = static_cast<int>((n_out + grid - 1) / grid);
+    const size_t part_bytes = (static_cast<size_t>(p.rows_cap) * wps * 4 + 15) & ~size_t(15);
+    const size_t ctrl = kStripMaxSlots * (8 + 4 + 4);
+    const size_t fixed = x_region_bytes(U) + part_bytes + ctrl;
+    if (fixed >= static_cast<size_t>(kMaxSmem)) return false;
+    const size_t budget = kMaxSmem - fixed;
+    // rows per slice per chunk: 4 (one 4-row group) when a chunk stays near
+    // 48 KB, else fewer
+    int m = static_cast<int>(49152 / (static_cast<size_t>(RS) * pitch));
+    if (m > 4) m = 4;
+    if (m < 1) m = 1;
+    const int max_m = (p.rows_cap + RS - 1) / RS;
+    if (m > max_m) m = max_m;
+    for (; m >= 1; --m) {
+        const int CR = RS * m;
+        const size_t stride = ((static_cast<size_t>(CR) * pitch + 15) & ~size_t(15)) + 32;
+        const int n_chunks = (p.rows_cap + CR - 1) / CR;
+        int slots = static_cast<int>(budget / stride);
+        if (slots > kStripMaxSlots) slots = kStripMaxSlots;
+        if (slots > n_chunks) slots = n_chunks;
+        if (slots >= 2 || (slots == 1 && n_chunks == 1)) {
+            p.chunk_rows = CR;
+            p.n_slots = slots;
+            p.slot_stride = static_cast<int>(stride);
+            p.smem = x_region_bytes(U) + slots * stride + part_bytes + ctrl;
+            return true;
+        }
+    }
+    return false;
+}
+
+template <int QT>
+cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
+                         const StripPlan& p, cudaStream_t stream) {
+    static int smem_set[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem_set[dev] < kMaxSmem) {
+        e = cudaFuncSetAttribute(qmv_strip_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        if (e != cudaSuccess) return e;
+        smem_set[dev] = kMaxSmem;
+    }
+    int* status = nullptr;
+    e = status_ptr(&status);
+    if (e != cudaSuccess) return e;
+    qmv_strip_kernel<QT><<<p.grid, kThreads, p.smem, stream>>>(w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
+                                                                p.slot_stride, p.rows_cap, status);
+    return cudaGetLastError();
+}
+
 template <int QT>
 cudaError_t launch_rowwise(const uint8_t* w, int n_out, int k, const float* x, int64_t ldx, int batch, float* y,
                            int64_t ldy, float scale, cudaStream_t stream) {
@@ -779,6 +1069,27 @@ cudaError_t qmv_stream(int qtype, const void* w, int64_t n_out, int64_t k, const
         case kQ4_K: return launch_stream<kQ4_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
         case kQ5_K: return launch_stream<kQ5_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
         case kQ6_K: return launch_stream<kQ6_K>(wb, n, kk, x, y, scale, counters, partials, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+bool qmv_strip_eligible(int qtype, const void* w, int64_t n_out, int64_t k) {
+    StripPlan p;
+    return (reinterpret_cast<uintptr_t>(w) % 16 == 0) && n_out < (int64_t(1) << 30) && plan_strip(qtype, n_out, k, p);
+}
+
+cudaError_t qmv_strip(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y, float scale,
+                      cudaStream_t stream) {
+    StripPlan p;
+    if (!plan_strip(qtype, n_out, k, p)) return cudaErrorInvalidValue;
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const int n = static_cast<int>(n_out), kk = static_cast<int>(k);
+    switch (qtype) {
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, stream);
         default: return cudaErrorInvalidValue;
     }
 }

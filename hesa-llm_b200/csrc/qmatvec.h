@@ -26,6 +26,11 @@ int64_t qmv_noalloc_max_rows();
 cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
                                float scale, cudaStream_t stream);
 
+// Row-strip batch-1 matvec (k <= 24576): CTAs own contiguous rows, no workspace.
+bool qmv_strip_eligible(int qtype, const void* w, int64_t n_out, int64_t k);
+cudaError_t qmv_strip(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y, float scale,
+                      cudaStream_t stream);
+
 // One warp per row, any k that is a multiple of the block size.
 cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,
                         int64_t batch, float* y, int64_t ldy, float scale, cudaStream_t stream);

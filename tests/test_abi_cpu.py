@@ -63,8 +63,9 @@ def call(qt=12, w=FAKE, n=64, k=256, x=FAKE, ldx=256, b=1, y=FAKE, ldy=64, ws=FA
     (dict(b=2, ldy=32), 6),
     (dict(w=FAKE + 8), 2),           # misaligned weights
     (dict(x=FAKE + 4), 2),           # misaligned activations
-    (dict(wsb=16), 2),               # workspace too small
-    (dict(ws=0), 2),
+    # k = 32768 takes the split-row kernel, the one that needs the workspace
+    (dict(k=32768, ldx=32768, wsb=16), 2),   # workspace too small
+    (dict(k=32768, ldx=32768, ws=0), 2),
 ])
 def test_qmatvec_rejects_bad_arguments_without_launching(kwargs, code):
     assert call(**kwargs) == code
