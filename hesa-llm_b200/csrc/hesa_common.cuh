@@ -76,14 +76,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may be suspended for up to `hint_ns`
+// while the phase is incomplete: it is woken when the phase completes, so a
+// waiting warp takes no issue slots from the warps that are decoding.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete. Returns false (and records
 // `code` in *status) if it has not completed within HESA_WAIT_LIMIT_NS.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_timer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 255u && global_timer_ns() - t0 > HESA_WAIT_LIMIT_NS) {
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;  // sleep up to 20 us per try
+        if (global_timer_ns() - t0 > HESA_WAIT_LIMIT_NS) {
             record_status(status, code);
             return false;
         }

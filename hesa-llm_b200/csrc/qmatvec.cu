@@ -715,12 +715,11 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         if (a1 > a0) bulk_g2s(dst, w + a0, static_cast<uint32_t>(a1 - a0), &full[slot]);
     };
 
-    if (threadIdx.x == 0)
-        for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
-
     // x as digit planes, converted once per CTA (one warp per unit of 256;
-    // the loads of a batch of units are issued together)
+    // the loads of a batch of units are issued together). Thread 0 primes the
+    // ring right after issuing its first x loads, so both are in flight at once.
     constexpr int kBatch = 4;
+    bool primed = false;
     for (int ub = warp; ub < U; ub += kWarps * kBatch) {
         float v[kBatch][8];
 #pragma unroll
@@ -733,12 +732,17 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
                 v[jb][4] = vb.x; v[jb][5] = vb.y; v[jb][6] = vb.z; v[jb][7] = vb.w;
             }
         }
+        if (!primed && threadIdx.x == 0)
+            for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
+        primed = true;
 #pragma unroll
         for (int jb = 0; jb < kBatch; ++jb) {
             const int u = ub + jb * kWarps;
             if (u < U) stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
         }
     }
+    if (!primed && threadIdx.x == 0)
+        for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
     __syncthreads();
 
     // this lane's quarter of x, in registers for every row it processes
