@@ -91,6 +91,24 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
     return ok != 0;
 }
 
+// Non-blocking: has phase `parity` of `bar` completed?
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Plain arrive (count 1) on `bar`; the arrival state is not needed.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Wait for phase `parity` of `bar` to complete. Returns false (and records
 // `code` in *status) if it has not completed within HESA_WAIT_LIMIT_NS.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int code) {
@@ -126,6 +144,13 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
         : "=l"(*reinterpret_cast<unsigned long long*>(&d))
         : "l"(*reinterpret_cast<const unsigned long long*>(&a)),
           "l"(*reinterpret_cast<const unsigned long long*>(&b)));
+    return d;
+}
+
+// max with NaN propagation (max.NaN.f32): a NaN in either input gives NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
     return d;
 }
 

@@ -113,6 +113,8 @@ struct XQuarter {
     uint32_t d[3][16];
     int ds[4][3];
     float s;
+    float s16;     // s / 16, for products taken on 16 x (high nibble in place)
+    float xs[2];   // sum_k x_k over groups 0 and 1 (K-quant min terms)
 };
 
 // Integer dot of 4 weight bytes (values that fit int8) with the 3 digit
@@ -121,6 +123,20 @@ __device__ __forceinline__ void dot3(uint32_t q, const XQuarter& xq, int w, int 
     p[0] = __dp4a(static_cast<int>(q), static_cast<int>(xq.d[0][w]), p[0]);
     p[1] = __dp4a(static_cast<int>(q), static_cast<int>(xq.d[1][w]), p[1]);
     p[2] = __dp4a(static_cast<int>(q), static_cast<int>(xq.d[2][w]), p[2]);
+}
+
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// As dot3 for unsigned weight bytes (0..255).
+__device__ __forceinline__ void dot3u(uint32_t q, const XQuarter& xq, int w, int (&p)[3]) {
+    p[0] = dp4a_us(q, xq.d[0][w], p[0]);
+    p[1] = dp4a_us(q, xq.d[1][w], p[1]);
+    p[2] = dp4a_us(q, xq.d[2][w], p[2]);
 }
 
 // 65536*a2 + 256*a1 + a0 in fp32.
@@ -162,14 +178,15 @@ __device__ __forceinline__ float unit_dot<kQ4_K>(const uint8_t* u, int c, const 
     int lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-        dot3(q[t] & 0x0F0F0F0Fu, xq, t, lo);          // sub-block 2c: indices 4t..4t+3
-        dot3((q[t] >> 4) & 0x0F0F0F0Fu, xq, 8 + t, hi);  // sub-block 2c+1: 32+4t..
+        dot3(q[t] & 0x0F0F0F0Fu, xq, t, lo);        // sub-block 2c: indices 4t..4t+3
+        dot3u(q[t] & 0xF0F0F0F0u, xq, 8 + t, hi);   // sub-block 2c+1 (32+4t..), as 16 q
     }
-    const int s0 = static_cast<int>(sc2 & 0xFF), s1 = static_cast<int>(sc2 >> 8);
-    const float t = combine3(s0 * lo[0] + s1 * hi[0], s0 * lo[1] + s1 * hi[1], s0 * lo[2] + s1 * hi[2]);
+    // 16 * (s0 * lo + s1 * q_hi . X): exact in int32 (|.| < 2^27)
+    const int s0x16 = static_cast<int>(sc2 & 0xFF) << 4, s1 = static_cast<int>(sc2 >> 8);
+    const float t = combine3(s0x16 * lo[0] + s1 * hi[0], s0x16 * lo[1] + s1 * hi[1], s0x16 * lo[2] + s1 * hi[2]);
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const float mins = fmaf(static_cast<float>(m2 & 0xFF), xsum(xq, 0), static_cast<float>(m2 >> 8) * xsum(xq, 1));
-    return fmaf(d * xq.s, t, -dmin * mins);
+    const float mins = fmaf(static_cast<float>(m2 & 0xFF), xq.xs[0], static_cast<float>(m2 >> 8) * xq.xs[1]);
+    return fmaf(d * xq.s16, t, -dmin * mins);
 }
 
 template <>
@@ -193,7 +210,7 @@ __device__ __forceinline__ float unit_dot<kQ5_K>(const uint8_t* u, int c, const 
     const int s0 = static_cast<int>(sc2 & 0xFF), s1 = static_cast<int>(sc2 >> 8);
     const float t = combine3(s0 * lo[0] + s1 * hi[0], s0 * lo[1] + s1 * hi[1], s0 * lo[2] + s1 * hi[2]);
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
-    const float mins = fmaf(static_cast<float>(m2 & 0xFF), xsum(xq, 0), static_cast<float>(m2 >> 8) * xsum(xq, 1));
+    const float mins = fmaf(static_cast<float>(m2 & 0xFF), xq.xs[0], static_cast<float>(m2 >> 8) * xq.xs[1]);
     return fmaf(d * xq.s, t, -dmin * mins);
 }
 
@@ -308,58 +325,98 @@ __device__ __forceinline__ int64_t owner_warp(int64_t c, int64_t C, int64_t W) {
 
 // Convert one unit (256 activations) to digit planes in shared memory; lane
 // L holds positions 8L..8L+7 in v.
+//
+// The balanced digits of X (|X| < 2^22) are the bytes of X + 0x808080, each
+// minus 128: adding 1.5 * 2^23 to x / s in one fused multiply-add rounds it to
+// the integer X (nearest, ties to even, as rint) in the low mantissa bits, so
+// X + 0x808080 is that float's bit pattern minus (0x4B400000 - 0x808080).
+// PRMT gathers byte p of four such words into digit-plane word p, and XOR
+// 0x80 per byte turns the biased bytes into signed digits.
 template <int QT>
 __device__ __forceinline__ void stage_unit(int unit, int lane, const float (&v)[8], uint8_t* xplanes, uint8_t* xsums,
                                            float* xscale) {
-    float am = 0.f;
-    bool nonfinite = false;
+    // largest magnitude: max.NaN keeps a NaN, inf compares above every finite
+    // value, and the bit patterns of non-negative floats order as integers
+    float fm = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        am = fmaxf(am, fabsf(v[j]));
-        nonfinite |= !(fabsf(v[j]) <= 3.402823466e38f);  // inf or NaN
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    for (int j = 0; j < 8; ++j) fm = fmax_nan(fm, fabsf(v[j]));
+    const uint32_t am = __reduce_max_sync(0xffffffffu, __float_as_uint(fm));
     // a non-finite activation makes the unit's scale NaN, so every output it
     // touches is NaN, as the fp32 reference sum would be inf or NaN
-    const bool finite = !__any_sync(0xffffffffu, nonfinite);
+    const bool finite = am < 0x7F800000u;
     // exponent E of the largest magnitude: |x| < 2^(E+1); s = 2^(E-21)
-    int E = static_cast<int>((__float_as_uint(am) >> 23) & 0xFFu) - 127;
+    int E = static_cast<int>(am >> 23) - 127;
     if (E < -100) E = -100;  // activations below 2^-100 round to zero
     const float inv_s = __uint_as_float(static_cast<uint32_t>(21 - E + 127) << 23);
     const float s = finite ? __uint_as_float(static_cast<uint32_t>(E - 21 + 127) << 23) : __int_as_float(0x7FC00000);
-    uint32_t dw[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+    // (digits of a non-finite unit are meaningless; its scale is NaN)
+    uint32_t Y[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int X = finite ? __float2int_rn(v[j] * inv_s) : 0;
-        const int d0 = (X << 24) >> 24;
-        const int X1 = (X - d0) >> 8;
-        const int d1 = (X1 << 24) >> 24;
-        const int d2 = (X1 - d1) >> 8;
-        const int sh = 8 * (j & 3);
-        dw[0][j >> 2] |= (static_cast<uint32_t>(d0) & 0xFFu) << sh;
-        dw[1][j >> 2] |= (static_cast<uint32_t>(d1) & 0xFFu) << sh;
-        dw[2][j >> 2] |= (static_cast<uint32_t>(d2) & 0xFFu) << sh;
+    for (int j = 0; j < 8; ++j) Y[j] = __float_as_uint(fmaf(v[j], inv_s, 12582912.0f)) - 0x4ABF7F80u;
+    uint32_t dw[3][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t* y = Y + 4 * h;
+        const uint32_t t01 = prmt(y[0], y[1], 0x5140u), t23 = prmt(y[2], y[3], 0x5140u);
+        const uint32_t u01 = prmt(y[0], y[1], 0x0062u), u23 = prmt(y[2], y[3], 0x0062u);
+        dw[0][h] = prmt(t01, t23, 0x5410u) ^ 0x80808080u;
+        dw[1][h] = prmt(t01, t23, 0x7632u) ^ 0x80808080u;
+        dw[2][h] = prmt(u01, u23, 0x5410u) ^ 0x80808080u;
     }
     int c, i0;
     unit_pos_to_slot<QT>(lane * 8, c, i0);
     uint8_t* qbase = xplanes + static_cast<size_t>(unit * 4 + c) * kQPlaneStride;
 #pragma unroll
     for (int p = 0; p < 3; ++p) *reinterpret_cast<uint2*>(qbase + p * 64 + i0) = make_uint2(dw[p][0], dw[p][1]);
+    // digit sums of the group (2 or 4 lanes): planes 0 and 1 travel packed in
+    // one word (each sum of at most 32 digits fits 16 bits signed)
     int sums[3];
 #pragma unroll
-    for (int p = 0; p < 3; ++p) {
+    for (int p = 0; p < 3; ++p)
         sums[p] = __dp4a(static_cast<int>(dw[p][0]), 0x01010101, __dp4a(static_cast<int>(dw[p][1]), 0x01010101, 0));
-        sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 1);
-        if constexpr (QT != kQ6_K) sums[p] += __shfl_xor_sync(0xffffffffu, sums[p], 2);
+    int s01 = sums[0] + (sums[1] << 16), s2 = sums[2];
+    s01 += __shfl_xor_sync(0xffffffffu, s01, 1);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+    if constexpr (QT != kQ6_K) {
+        s01 += __shfl_xor_sync(0xffffffffu, s01, 2);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
     }
     const bool writer = (QT == kQ6_K) ? ((lane & 1) == 0) : ((lane & 3) == 0);
     if (writer) {
+        const int s0 = static_cast<int>(static_cast<int16_t>(s01 & 0xFFFF));
         int* ds = reinterpret_cast<int*>(xsums + static_cast<size_t>(unit * 4 + c) * kQSumStride) +
                   4 * (i0 >> group_shift<QT>());
-        *reinterpret_cast<int4*>(ds) = make_int4(sums[0], sums[1], sums[2], 0);
+        *reinterpret_cast<int4*>(ds) = make_int4(s0, (s01 - s0) >> 16, s2, 0);
     }
     if (lane == 0) xscale[unit] = s;
+}
+
+// The activations of quarter qc of `unit`, from the staged planes into registers.
+template <int QT>
+__device__ __forceinline__ void load_xquarter(const uint8_t* xplanes, const uint8_t* xsums, const float* xscale,
+                                              int unit, int qc, XQuarter& xq) {
+    const uint8_t* qsrc = xplanes + static_cast<size_t>(unit * 4 + qc) * kQPlaneStride;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint4 w4 = lds128(qsrc + p * 64 + 16 * t);
+            xq.d[p][4 * t] = w4.x; xq.d[p][4 * t + 1] = w4.y;
+            xq.d[p][4 * t + 2] = w4.z; xq.d[p][4 * t + 3] = w4.w;
+        }
+    }
+    const uint8_t* ssrc = xsums + static_cast<size_t>(unit * 4 + qc) * kQSumStride;
+#pragma unroll
+    for (int gg = 0; gg < (QT == kQ6_K ? 4 : 2); ++gg) {
+        const int4 s4 = *reinterpret_cast<const int4*>(ssrc + 16 * gg);
+        xq.ds[gg][0] = s4.x; xq.ds[gg][1] = s4.y; xq.ds[gg][2] = s4.z;
+    }
+    xq.s = xscale[unit];
+    xq.s16 = xq.s * 0.0625f;
+    if constexpr (QT == kQ4_K || QT == kQ5_K) {
+        xq.xs[0] = xsum(xq, 0);
+        xq.xs[1] = xsum(xq, 1);
+    }
 }
 
 template <int QT>
@@ -501,23 +558,7 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
             const int unit = u0 + ju;
             // this lane's activations, kept in registers for the R rows
             XQuarter xq;
-            const uint8_t* qsrc = xplanes + static_cast<size_t>(unit * 4 + qc) * kQPlaneStride;
-#pragma unroll
-            for (int p = 0; p < 3; ++p) {
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const uint4 w4 = lds128(qsrc + p * 64 + 16 * t);
-                    xq.d[p][4 * t] = w4.x; xq.d[p][4 * t + 1] = w4.y;
-                    xq.d[p][4 * t + 2] = w4.z; xq.d[p][4 * t + 3] = w4.w;
-                }
-            }
-            const uint8_t* ssrc = xsums + static_cast<size_t>(unit * 4 + qc) * kQSumStride;
-#pragma unroll
-            for (int gg = 0; gg < (QT == kQ6_K ? 4 : 2); ++gg) {
-                const int4 s4 = *reinterpret_cast<const int4*>(ssrc + 16 * gg);
-                xq.ds[gg][0] = s4.x; xq.ds[gg][1] = s4.y; xq.ds[gg][2] = s4.z;
-            }
-            xq.s = xscale[unit];
+            load_xquarter<QT>(xplanes, xsums, xscale, unit, qc, xq);
             const size_t base = static_cast<size_t>(g) * R * pitch + static_cast<size_t>(u0) * UB;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
@@ -609,12 +650,14 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
 //   * CTA b owns the contiguous rows [b*n_out/G, (b+1)*n_out/G) (balanced to
 //     one row). Its bytes are one contiguous range of W, streamed as chunks of
 //     chunk_rows whole rows, one cp.async.bulk per chunk, into a ring of up to
-//     kStripMaxSlots shared-memory slots; for decode-size matrices the whole
-//     range is in flight from the first microsecond.
+//     kStripMaxSlots shared-memory slots; most of the range is in flight
+//     from the first microsecond.
+//   * x is converted to digit planes once per CTA (one warp per unit of 256)
+//     while the first copies are in flight.
 //   * Lane (slice s, quarter-column q) owns 64 weights of every row r with
-//     r = s (mod slices): unit q/4, quarter q%4. It builds that quarter of x as
-//     digit planes once, straight from global memory, and keeps it in
-//     registers for all its rows. Whole warps belong to one slice.
+//     r = s (mod slices): unit q/4, quarter q%4. It loads that quarter of x
+//     once and keeps it in registers for all its rows. Whole warps belong to
+//     one slice.
 //   * Per row, a warp's lanes are reduced with shuffles and lane 0 stores
 //     the warp's partial in shared memory; at the end the CTA adds the warps'
 //     partials of each row in a fixed order. No workspace, deterministic.
@@ -642,6 +685,14 @@ __device__ __forceinline__ float reduce4(const float (&v)[4], int lane) {
     c += __shfl_xor_sync(0xffffffffu, c, 2);
     c += __shfl_xor_sync(0xffffffffu, c, 1);
     return c;
+}
+
+// Quarter qc of rows rb, rb + rstep, ... (NR of them) against the lane's x.
+template <int QT, int NR>
+__device__ __forceinline__ void strip_rows(const uint8_t* rb, size_t rstep, int qc, const XQuarter& xq,
+                                           float (&a)[4]) {
+#pragma unroll
+    for (int t = 0; t < NR; ++t) a[t] = unit_dot<QT>(rb + t * rstep, qc, xq);
 }
 
 template <int QT>
@@ -717,9 +768,10 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
 
     // x as digit planes, converted once per CTA (one warp per unit of 256;
     // the loads of a batch of units are issued together). Thread 0 primes the
-    // ring right after issuing its first x loads, so both are in flight at once.
-    constexpr int kBatch = 4;
+    // ring as soon as its own x loads have landed: x reaches the SMs faster
+    // while the copy engine is still idle.
     bool primed = false;
+    constexpr int kBatch = 4;
     for (int ub = warp; ub < U; ub += kWarps * kBatch) {
         float v[kBatch][8];
 #pragma unroll
@@ -732,7 +784,8 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
                 v[jb][4] = vb.x; v[jb][5] = vb.y; v[jb][6] = vb.z; v[jb][7] = vb.w;
             }
         }
-        if (!primed && threadIdx.x == 0)
+        // (the branch reads a loaded value, so it waits for thread 0's loads)
+        if (threadIdx.x == 0 && !primed && __float_as_uint(v[0][0]) != 0xFFFFFFFFu)
             for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
         primed = true;
 #pragma unroll
@@ -741,31 +794,13 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
             if (u < U) stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
         }
     }
-    if (!primed && threadIdx.x == 0)
+    if (threadIdx.x == 0 && !primed)
         for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
     __syncthreads();
 
     // this lane's quarter of x, in registers for every row it processes
     XQuarter xq;
-    if (qactive) {
-        const uint8_t* qsrc = xplanes + static_cast<size_t>(unit * 4 + qc) * kQPlaneStride;
-#pragma unroll
-        for (int p = 0; p < 3; ++p) {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const uint4 w4 = lds128(qsrc + p * 64 + 16 * t);
-                xq.d[p][4 * t] = w4.x; xq.d[p][4 * t + 1] = w4.y;
-                xq.d[p][4 * t + 2] = w4.z; xq.d[p][4 * t + 3] = w4.w;
-            }
-        }
-        const uint8_t* ssrc = xsums + static_cast<size_t>(unit * 4 + qc) * kQSumStride;
-#pragma unroll
-        for (int gg = 0; gg < (QT == kQ6_K ? 4 : 2); ++gg) {
-            const int4 s4 = *reinterpret_cast<const int4*>(ssrc + 16 * gg);
-            xq.ds[gg][0] = s4.x; xq.ds[gg][1] = s4.y; xq.ds[gg][2] = s4.z;
-        }
-        xq.s = xscale[unit];
-    }
+    if (qactive) load_xquarter<QT>(xplanes, xsums, xscale, unit, qc, xq);
 
     bool failed = false;
     if (wactive) {
@@ -782,13 +817,19 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
             const uint8_t* base = slots + static_cast<size_t>(slot) * slot_stride +
                                   ((static_cast<size_t>(r0 + lr0) * pitch) & 15) + static_cast<size_t>(unit) * UB;
             // this slice's rows of the chunk, four at a time: independent
-            // decode chains, then one transposing reduction for the four
+            // decode chains, then one transposing reduction for the four.
+            // The row count of a group is warp-uniform; each count has its
+            // own code so no decode is issued for a missing row.
             for (int i0 = lr0 + slice; i0 < lr1; i0 += 4 * RS) {
-                float a[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int i = i0 + t * RS;
-                    a[t] = (qactive && i < lr1) ? unit_dot<QT>(base + static_cast<size_t>(i - lr0) * pitch, qc, xq) : 0.f;
+                float a[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint8_t* rb = base + static_cast<size_t>(i0 - lr0) * pitch;
+                const size_t rstep = static_cast<size_t>(RS) * pitch;
+                const int nv = (lr1 - i0 + RS - 1) / RS;
+                if (qactive) {
+                    if (nv >= 4) strip_rows<QT, 4>(rb, rstep, qc, xq, a);
+                    else if (nv == 3) strip_rows<QT, 3>(rb, rstep, qc, xq, a);
+                    else if (nv == 2) strip_rows<QT, 2>(rb, rstep, qc, xq, a);
+                    else strip_rows<QT, 1>(rb, rstep, qc, xq, a);
                 }
                 const int row = i0 + RS * reduce4_row(lane);
                 const float tot = reduce4(a, lane);
@@ -930,7 +971,7 @@ struct StripPlan {
 };
 
 // Launch geometry of the row-strip kernel: one CTA per SM (at most one per
-// row), chunks of a multiple of the row-slice count near 24 KB, and as many
+// row), chunks of up to four rows per row slice (at most 56 KB), and as many
 // ring slots as shared memory holds (no more than the CTA has chunks).
 bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
     if (!qtype_supported(qt) || k % 256 != 0 || n_out < 1) return false;
@@ -948,9 +989,9 @@ bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
     const size_t fixed = x_region_bytes(U) + part_bytes + ctrl;
     if (fixed >= static_cast<size_t>(kMaxSmem)) return false;
     const size_t budget = kMaxSmem - fixed;
-    // rows per slice per chunk: 4 (one 4-row group) when a chunk stays near
-    // 48 KB, else fewer
-    int m = static_cast<int>(49152 / (static_cast<size_t>(RS) * pitch));
+    // rows per slice per chunk: 4 (one 4-row group) when a chunk stays within
+    // 56 KB, else fewer
+    int m = static_cast<int>(57344 / (static_cast<size_t>(RS) * pitch));
     if (m > 4) m = 4;
     if (m < 1) m = 1;
     const int max_m = (p.rows_cap + RS - 1) / RS;
