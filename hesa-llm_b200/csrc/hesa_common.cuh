@@ -147,6 +147,14 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return d;
 }
 
+// Programmatic dependent launch. grid_dep_wait blocks until the grids this one
+// depends on (the previous kernel on the stream, when launched with
+// programmatic stream serialization) have completed and their writes are
+// visible; grid_dep_launch lets the next such kernel start its CTAs as SMs
+// free up. Both are no-ops for a normal launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // max with NaN propagation (max.NaN.f32): a NaN in either input gives NaN.
 __device__ __forceinline__ float fmax_nan(float a, float b) {
     float d;

@@ -766,11 +766,15 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         if (a1 > a0) bulk_g2s(dst, w + a0, static_cast<uint32_t>(a1 - a0), &full[slot]);
     };
 
+    // The weights never come from the previous kernel on the stream, so the
+    // ring is primed before waiting for it; x may, so it is read after.
+    if (threadIdx.x == 0)
+        for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
+    grid_dep_launch();
+    grid_dep_wait();
+
     // x as digit planes, converted once per CTA (one warp per unit of 256;
-    // the loads of a batch of units are issued together). Thread 0 primes the
-    // ring as soon as its own x loads have landed: x reaches the SMs faster
-    // while the copy engine is still idle.
-    bool primed = false;
+    // the loads of a batch of units are issued together)
     constexpr int kBatch = 4;
     for (int ub = warp; ub < U; ub += kWarps * kBatch) {
         float v[kBatch][8];
@@ -784,18 +788,12 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
                 v[jb][4] = vb.x; v[jb][5] = vb.y; v[jb][6] = vb.z; v[jb][7] = vb.w;
             }
         }
-        // (the branch reads a loaded value, so it waits for thread 0's loads)
-        if (threadIdx.x == 0 && !primed && __float_as_uint(v[0][0]) != 0xFFFFFFFFu)
-            for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
-        primed = true;
 #pragma unroll
         for (int jb = 0; jb < kBatch; ++jb) {
             const int u = ub + jb * kWarps;
             if (u < U) stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
         }
     }
-    if (threadIdx.x == 0 && !primed)
-        for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
     __syncthreads();
 
     // this lane's quarter of x, in registers for every row it processes
@@ -1030,9 +1028,20 @@ cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, flo
     int* status = nullptr;
     e = status_ptr(&status);
     if (e != cudaSuccess) return e;
-    qmv_strip_kernel<QT><<<p.grid, kThreads, p.smem, stream>>>(w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
-                                                                p.slot_stride, p.rows_cap, status);
-    return cudaGetLastError();
+    // programmatic stream serialization: the CTAs may start while the previous
+    // kernel on the stream finishes; the kernel waits for it before reading x
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, qmv_strip_kernel<QT>, w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
+                              p.slot_stride, p.rows_cap, status);
 }
 
 template <int QT>
