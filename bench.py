@@ -79,9 +79,9 @@ def measured_peaks():
 
 
 def committed_traffic():
-    """Per-step DRAM bytes of the streaming kernels from the committed ncu
-    summary (profiles/qmv_stream_sweep_traffic.json), or None."""
-    p = os.path.join(ROOT, "profiles", "qmv_stream_sweep_traffic.json")
+    """Per-step DRAM bytes of the batch-1 matvec kernels from the committed ncu
+    summary (profiles/qmv_strip_sweep_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "qmv_strip_sweep_traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as f:
@@ -460,7 +460,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                          "traffic": traffic,
-                         "kernel": "qmv_stream_kernel (8 launches per step)"},
+                         "kernel": "qmv_strip_kernel (8 launches per step)"},
             "per_type_gbs": per_type,
             "pct_of_8tbs": round(achieved / 8000.0, 4),
             "e2e": {"value": round(bytes_step * args.steps / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",

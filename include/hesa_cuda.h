@@ -77,8 +77,16 @@ HESA_CUDA_API size_t hesa_cuda_qmatvec_workspace_size(int qtype, int64_t n_out, 
  * TensorView b, TensorView out, float scale) (include/hesa/backend.hpp:43-44)
  * whose CPU semantics are cpu_matmul_f32 (src/backend/cpu_backend.cpp:24-41):
  * a = W [n_out, k], b = x^T [k, batch], out = y^T [n_out, batch].
- * batch >= 8 runs on the tensor-core tile path; smaller batches on CUDA cores.
- * x and y must be 16-byte aligned with ldx, ldy multiples of 4. */
+ * Each batch column is one streaming pass over W on CUDA cores.
+ * x and y must be 16-byte aligned with ldx, ldy multiples of 4.
+ * The workspace is used only by the split-row kernel (rows longer than 24576
+ * weights, or matrices too tall for one strip of rows per SM); a call that
+ * needs it and gets less than hesa_cuda_qmatvec_workspace_size bytes fails
+ * with HESA_CUDA_INVALID_ARGUMENT before launching anything.
+ * Consecutive calls on one stream overlap (programmatic dependent launch):
+ * a call starts fetching W while the previous kernel on the stream finishes,
+ * and reads x only after that kernel has completed. W must therefore not be
+ * written by the kernel launched immediately before the call. */
 HESA_CUDA_API int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int64_t k,
                                     const float* x, int64_t ldx, int64_t batch,
                                     float* y, int64_t ldy, float scale,
