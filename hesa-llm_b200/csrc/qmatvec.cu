@@ -767,9 +767,11 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     };
 
     // The weights never come from the previous kernel on the stream, so the
-    // ring is primed before waiting for it; x may, so it is read after.
-    if (threadIdx.x == 0)
-        for (int j = 0; j < n_slots && j < n_chunks; ++j) issue(j);
+    // first chunk is fetched before waiting for it; x may, so it is read
+    // after. The other slots are filled once x is staged: a flood of incoming
+    // copies during the staging slows the staging more than it gains
+    // (measured: 9.25 vs 10.45 us for a 4096x11008 Q4_K launch).
+    if (threadIdx.x == 0) issue(0);
     grid_dep_launch();
     grid_dep_wait();
 
@@ -794,6 +796,8 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
             if (u < U) stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
         }
     }
+    if (threadIdx.x == 0)
+        for (int j = 1; j < n_slots && j < n_chunks; ++j) issue(j);
     __syncthreads();
 
     // this lane's quarter of x, in registers for every row it processes
