@@ -5,7 +5,9 @@
 // launch nothing. CUDA errors map to HESA_CUDA_ERROR with the message kept
 // per host thread.
 #include "../../include/hesa_cuda.h"
+#include "abi_errors.h"
 #include "qmatvec.h"
+#include "quantize.h"
 #include "qtypes.cuh"
 
 #include <string>
@@ -27,6 +29,11 @@ int cuda_fail(cudaError_t e, const char* where) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+namespace hesa_cuda {
+int record_error(int code, const char* what) { return fail(code, what); }
+int record_cuda_error(cudaError_t e, const char* where) { return cuda_fail(e, where); }
+}  // namespace hesa_cuda
 
 extern "C" {
 
@@ -91,6 +98,17 @@ int hesa_cuda_dequantize(int qtype, const void* w, int64_t n_rows, int64_t k, fl
         return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
     cudaError_t e = hesa_cuda::dequantize(qtype, w, n_rows, k, out, ldo, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "dequantize kernel");
+    return HESA_CUDA_OK;
+}
+
+int hesa_cuda_quantize(int qtype, const float* src, int64_t n_rows, int64_t k, int64_t ld_src, void* dst,
+                       void* stream) {
+    if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
+    if (!src || !dst) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n_rows <= 0 || k <= 0 || k % hesa_cuda::block_elems(qtype) != 0 || ld_src < k)
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
+    cudaError_t e = hesa_cuda::quantize(qtype, src, n_rows, k, ld_src, dst, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "quantize kernel");
     return HESA_CUDA_OK;
 }
 
@@ -188,12 +206,14 @@ int hesa_cuda_rope_table(float* table_host, int32_t n_pos, int64_t head_dim, flo
     return HESA_CUDA_OK;
 }
 
-int hesa_cuda_rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, const int32_t* pos_dev,
-                   int32_t pos_host, void* stream) {
+int hesa_cuda_rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, int32_t table_rows,
+                   const int32_t* pos_dev, int32_t pos_host, void* stream) {
     if (!data || !table) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
-    if (n_heads <= 0 || head_dim <= 0 || (head_dim & 1) || (!pos_dev && pos_host < 0))
+    if (n_heads <= 0 || head_dim <= 0 || (head_dim & 1) || table_rows <= 0 ||
+        (!pos_dev && (pos_host < 0 || pos_host >= table_rows)))
         return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
-    cudaError_t e = hesa_cuda::rope(data, n_heads, head_dim, table, pos_dev, pos_host, static_cast<cudaStream_t>(stream));
+    cudaError_t e = hesa_cuda::rope(data, n_heads, head_dim, table, table_rows, pos_dev, pos_host,
+                                    static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "rope");
 }
 

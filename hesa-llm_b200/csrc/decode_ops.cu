@@ -16,6 +16,7 @@
 // replayed for every token.
 #include "hesa_common.cuh"
 #include "decode_ops.h"
+#include "qmatvec.h"
 
 #include <cuda/atomic>
 #include <cuda_fp16.h>
@@ -117,9 +118,14 @@ softmax_kernel(const float* __restrict__ in, float* __restrict__ out, int n) {
 
 // data [n_heads, head_dim]; table row p holds cos[half] then sin[half]
 __global__ void rope_kernel(float* __restrict__ data, int n_heads, int head_dim, const float* __restrict__ table,
-                            const int32_t* __restrict__ pos_dev, int32_t pos_host) {
+                            int table_rows, const int32_t* __restrict__ pos_dev, int32_t pos_host,
+                            int* __restrict__ status) {
     const int half = head_dim >> 1;
     const int32_t pos = pos_dev ? *pos_dev : pos_host;
+    if (pos < 0 || pos >= table_rows) {   // no row of the table: leave data as is
+        if (blockIdx.x == 0 && threadIdx.x == 0) record_status(status, kStatusBadPosition);
+        return;
+    }
     const float* cs = table + static_cast<int64_t>(pos) * head_dim;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_heads * half; i += gridDim.x * blockDim.x) {
         const int h = i / half, d = i - h * half;
@@ -134,8 +140,12 @@ __global__ void rope_kernel(float* __restrict__ data, int n_heads, int head_dim,
 
 __global__ void kv_store_kernel(const float* __restrict__ k, const float* __restrict__ v, __half* __restrict__ kc,
                                 __half* __restrict__ vc, int row_elems, int ctx, const int32_t* __restrict__ pos_dev,
-                                int32_t pos_host) {
+                                int32_t pos_host, int* __restrict__ status) {
     const int32_t pos = pos_dev ? *pos_dev : pos_host;
+    if (pos < 0) {   // no slot: write nothing
+        if (blockIdx.x == 0 && threadIdx.x == 0) record_status(status, kStatusBadPosition);
+        return;
+    }
     const int64_t slot = pos % ctx;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row_elems; i += gridDim.x * blockDim.x) {
         kc[slot * row_elems + i] = __float2half_rn(k[i]);
@@ -290,19 +300,25 @@ cudaError_t softmax(const float* in, float* out, int64_t n_rows, int64_t n, cuda
     return cudaGetLastError();
 }
 
-cudaError_t rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, const int32_t* pos_dev,
-                 int32_t pos_host, cudaStream_t s) {
+cudaError_t rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, int32_t table_rows,
+                 const int32_t* pos_dev, int32_t pos_host, cudaStream_t s) {
+    int* status = nullptr;
+    cudaError_t e = status_word(&status);
+    if (e != cudaSuccess) return e;
     rope_kernel<<<grid_for(n_heads * head_dim / 2, 256, 64), 256, 0, s>>>(
-        data, static_cast<int>(n_heads), static_cast<int>(head_dim), table, pos_dev, pos_host);
+        data, static_cast<int>(n_heads), static_cast<int>(head_dim), table, table_rows, pos_dev, pos_host, status);
     return cudaGetLastError();
 }
 
 cudaError_t kv_store(const float* k, const float* v, void* kc, void* vc, int64_t row_elems, int64_t ctx,
                      const int32_t* pos_dev, int32_t pos_host, cudaStream_t s) {
+    int* status = nullptr;
+    cudaError_t e = status_word(&status);
+    if (e != cudaSuccess) return e;
     kv_store_kernel<<<grid_for(row_elems, 256, 64), 256, 0, s>>>(k, v, static_cast<__half*>(kc),
                                                                   static_cast<__half*>(vc),
                                                                   static_cast<int>(row_elems),
-                                                                  static_cast<int>(ctx), pos_dev, pos_host);
+                                                                  static_cast<int>(ctx), pos_dev, pos_host, status);
     return cudaGetLastError();
 }
 

@@ -15,8 +15,8 @@ cudaError_t silu_mul(const float* g, const float* u, float* o, int64_t n, cudaSt
 cudaError_t binary(const float* a, const float* b, float* o, int64_t n, int op /*0 add, 1 mul*/,
                    cudaStream_t s);
 cudaError_t softmax(const float* in, float* out, int64_t n_rows, int64_t n, cudaStream_t s);
-cudaError_t rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, const int32_t* pos_dev,
-                 int32_t pos_host, cudaStream_t s);
+cudaError_t rope(float* data, int64_t n_heads, int64_t head_dim, const float* table, int32_t table_rows,
+                 const int32_t* pos_dev, int32_t pos_host, cudaStream_t s);
 cudaError_t kv_store(const float* k, const float* v, void* kc, void* vc, int64_t row_elems, int64_t ctx,
                      const int32_t* pos_dev, int32_t pos_host, cudaStream_t s);
 int attention_splits(int64_t ctx);

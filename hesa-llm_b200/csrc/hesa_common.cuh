@@ -17,6 +17,7 @@ namespace hesa_cuda {
 enum : int {
     kStatusWaitTimeout = 1,     // a stage's bulk copy did not land in time
     kStatusDrainTimeout = 2,    // a copy still in flight during the error exit
+    kStatusBadPosition = 3,     // a device-side position outside the cache / rope table
 };
 
 constexpr unsigned long long HESA_WAIT_LIMIT_NS = 2000000000ull;  // 2 s

@@ -1230,6 +1230,8 @@ cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t 
     }
 }
 
+cudaError_t status_word(int** out) { return status_ptr(out); }
+
 cudaError_t read_device_status(int* out) {
     return cudaMemcpyFromSymbol(out, g_hesa_status, sizeof(int));
 }

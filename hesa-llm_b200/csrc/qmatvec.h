@@ -37,6 +37,9 @@ cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, cons
 
 // Sticky status word of the bounded waits (0 = healthy).
 cudaError_t read_device_status(int* out);
+// Device address of the library's status word on the current device (kernels
+// of other files record their failures there too).
+cudaError_t status_word(int** out);
 cudaError_t clear_device_status(cudaStream_t stream);
 
 cudaError_t dequantize(int qtype, const void* w, int64_t n_rows, int64_t k, float* out, int64_t ldo,

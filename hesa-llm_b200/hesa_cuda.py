@@ -27,6 +27,21 @@ ERRORS = {0: "SUCCESS", 1: "OUT_OF_MEMORY", 2: "INVALID_ARGUMENT", 3: "BACKEND_N
 
 # (name, restype, argtypes) of every function include/hesa_cuda.h declares
 _vp, _i64, _sz, _int, _f = ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t, ctypes.c_int, ctypes.c_float
+
+
+class Model(ctypes.Structure):
+    """hesa_cuda_model (include/hesa_cuda.h)."""
+    _fields_ = [("n_layer", ctypes.c_int32), ("d_model", ctypes.c_int32), ("n_head", ctypes.c_int32),
+                ("n_kv_head", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("d_ff", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("ctx", ctypes.c_int32), ("rms_eps", ctypes.c_float),
+                ("rope_base", ctypes.c_float), ("qtype", ctypes.c_int32)]
+
+
+class Layer(ctypes.Structure):
+    """hesa_cuda_layer (include/hesa_cuda.h): device pointers of one layer."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down", "attn_norm",
+                                              "ffn_norm", "k_cache", "v_cache")]
+
 SIGNATURES = [
     ("hesa_cuda_version", ctypes.c_char_p, []),
     ("hesa_cuda_row_bytes", _sz, [_int, _i64]),
@@ -34,6 +49,7 @@ SIGNATURES = [
     ("hesa_cuda_qmatvec", _int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _f, _vp, _sz, _vp]),
     ("hesa_cuda_qmatvec_noalloc", _int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _f, _vp]),
     ("hesa_cuda_dequantize", _int, [_int, _vp, _i64, _i64, _vp, _i64, _vp]),
+    ("hesa_cuda_quantize", _int, [_int, _vp, _i64, _i64, _i64, _vp, _vp]),
     ("hesa_cuda_device_status", _int, [_vp, ctypes.POINTER(_int)]),
     ("hesa_cuda_clear_device_status", _int, [_vp]),
     ("hesa_cuda_last_error", ctypes.c_char_p, []),
@@ -44,11 +60,15 @@ SIGNATURES = [
     ("hesa_cuda_mul", _int, [_vp, _vp, _vp, _i64, _vp]),
     ("hesa_cuda_softmax", _int, [_vp, _vp, _i64, _i64, _vp]),
     ("hesa_cuda_rope_table", _int, [_vp, ctypes.c_int32, _i64, _f]),
-    ("hesa_cuda_rope", _int, [_vp, _i64, _i64, _vp, _vp, ctypes.c_int32, _vp]),
+    ("hesa_cuda_rope", _int, [_vp, _i64, _i64, _vp, ctypes.c_int32, _vp, ctypes.c_int32, _vp]),
     ("hesa_cuda_kv_store", _int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, ctypes.c_int32, _vp]),
     ("hesa_cuda_attention_workspace_size", _sz, [_i64, _i64, _i64]),
     ("hesa_cuda_attention", _int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, ctypes.c_int32, _vp, _sz,
                                    _vp]),
+    ("hesa_cuda_decode_workspace_size", _sz, [ctypes.POINTER(Model)]),
+    ("hesa_cuda_embed", _int, [_int, _vp, _i64, _i64, _vp, _vp, _vp]),
+    ("hesa_cuda_decode_step", _int, [ctypes.POINTER(Model), ctypes.POINTER(Layer), _vp, _vp, _vp, ctypes.c_int32,
+                                     _vp, _vp, _vp, _vp, _sz, _vp]),
 ]
 
 
@@ -136,6 +156,24 @@ def dequantize(qtype: int, w, k: int, out=None, stream=None):
         out = torch.empty((n_rows, k), dtype=torch.float32, device=w.device)
     _check(lib().hesa_cuda_dequantize(qtype, w.data_ptr(), n_rows, k, out.data_ptr(), out.stride(0),
                                       _stream_handle(stream)))
+    return out
+
+
+def quantize(qtype: int, x, out=None, stream=None):
+    """Packed GGUF rows [n_rows, row_bytes] (uint8, CUDA) of fp32 x [n_rows, k]
+    (CUDA), deterministic round-to-nearest (hesa_cuda_quantize)."""
+    import torch
+    x2 = x.unsqueeze(0) if x.dim() == 1 else x
+    n_rows, k = x2.shape
+    if x2.stride(1) != 1:
+        raise ValueError("rows of x must be contiguous")
+    rb = row_bytes(qtype, k)
+    if rb == 0:
+        raise HesaError(6, f"k={k} is not a multiple of the block size of qtype {qtype}")
+    if out is None:
+        out = torch.empty((n_rows, rb), dtype=torch.uint8, device=x.device)
+    _check(lib().hesa_cuda_quantize(qtype, x2.data_ptr(), n_rows, k, x2.stride(0), out.data_ptr(),
+                                    _stream_handle(stream)))
     return out
 
 
@@ -231,8 +269,8 @@ def rope_table(n_pos: int, head_dim: int, base: float = 10000.0):
 
 
 def rope(x, n_heads: int, head_dim: int, table, pos=None, pos_dev=None, stream=None):
-    _check(lib().hesa_cuda_rope(x.data_ptr(), n_heads, head_dim, table.data_ptr(), _ptr(pos_dev),
-                                int(pos or 0), _stream_handle(stream)))
+    _check(lib().hesa_cuda_rope(x.data_ptr(), n_heads, head_dim, table.data_ptr(), table.shape[0],
+                                _ptr(pos_dev), int(pos or 0), _stream_handle(stream)))
     return x
 
 
@@ -257,3 +295,45 @@ def attention(q, k_cache, v_cache, n_head: int, n_kv_head: int, head_dim: int, c
                                      n_kv_head, head_dim, ctx, _ptr(pos_dev), int(pos or 0), workspace.data_ptr(),
                                      workspace.numel(), _stream_handle(stream)))
     return out
+
+
+# ---------------------------------------------------------------------------
+# decode step
+# ---------------------------------------------------------------------------
+
+def decode_workspace(model: Model, device=None):
+    """Zero-filled workspace of hesa_cuda_decode_step (uint8, 256-byte aligned)."""
+    import torch
+    nb = int(lib().hesa_cuda_decode_workspace_size(ctypes.byref(model)))
+    if nb == 0:
+        raise HesaError(6, "bad model shape")
+    return torch.zeros(nb, dtype=torch.uint8, device=device or "cuda")
+
+
+def embed(qtype: int, w_emb, d_model: int, token_dev, out=None, stream=None):
+    import torch
+    out = torch.empty(d_model, dtype=torch.float32, device=w_emb.device) if out is None else out
+    _check(lib().hesa_cuda_embed(qtype, w_emb.data_ptr(), w_emb.shape[0], d_model, token_dev.data_ptr(),
+                                 out.data_ptr(), _stream_handle(stream)))
+    return out
+
+
+def decode_step(model: Model, layers, out_norm, w_out, rope_table, x_embed, pos_dev, logits, workspace,
+                stream=None):
+    """One token through the decoder (hesa_cuda_decode_step). `layers` is a
+    ctypes array of Layer (see make_layers)."""
+    _check(lib().hesa_cuda_decode_step(ctypes.byref(model), layers, out_norm.data_ptr(), w_out.data_ptr(),
+                                       rope_table.data_ptr(), rope_table.shape[0], x_embed.data_ptr(),
+                                       pos_dev.data_ptr(), logits.data_ptr(), workspace.data_ptr(),
+                                       workspace.numel(), _stream_handle(stream)))
+    return logits
+
+
+def make_layers(per_layer):
+    """ctypes array of Layer from a list of dicts of CUDA tensors with the
+    keys of Layer's fields."""
+    arr = (Layer * len(per_layer))()
+    for i, d in enumerate(per_layer):
+        for name, _ in Layer._fields_:
+            setattr(arr[i], name, d[name].data_ptr())
+    return arr

@@ -122,6 +122,17 @@ HESA_CUDA_API int hesa_cuda_qmatvec_noalloc(int qtype, const void* w, int64_t n_
 HESA_CUDA_API int hesa_cuda_dequantize(int qtype, const void* w, int64_t n_rows, int64_t k,
                                        float* out, int64_t ldo, void* stream);
 
+/* dst <- src [n_rows, k] fp32 (row stride ld_src floats) quantized to
+ * packed GGUF rows of qtype (n_rows * hesa_cuda_row_bytes(qtype, k) bytes),
+ * deterministic round-to-nearest: Q4_0 / Q8_0 with the published ggml
+ * reference rounding, the K-quants with a min/max RTN (6-bit sub-block
+ * scale/min for Q4_K, Q5_K; int8 sub-block scales for Q6_K). The device
+ * side of the block codec; the reference declares Backend::quantize
+ * (include/hesa/backend.hpp:60) and leaves it unimplemented on the CPU
+ * (src/backend/cpu_backend.cpp:296-302). src and dst are device pointers. */
+HESA_CUDA_API int hesa_cuda_quantize(int qtype, const float* src, int64_t n_rows, int64_t k, int64_t ld_src,
+                                     void* dst, void* stream);
+
 /* ---------------------------------------------------------------------
  * Decode-step helpers (single token). Semantics of hesa-llm's CPU kernels,
  * src/backend/cpu_backend.cpp; `pos` arguments are a device int32 scalar
@@ -162,14 +173,18 @@ HESA_CUDA_API int hesa_cuda_softmax(const float* in, float* out, int64_t n_rows,
 HESA_CUDA_API int hesa_cuda_rope_table(float* table_host, int32_t n_pos, int64_t head_dim, float freq_base);
 
 /* In-place rotate-half RoPE of data [n_heads, head_dim] at position pos,
- * from a device copy of hesa_cuda_rope_table (cpu_rope_f32,
- * cpu_backend.cpp:98-120; Backend::rope, backend.hpp:50-51). */
+ * from a device copy of hesa_cuda_rope_table with table_rows rows
+ * (cpu_rope_f32, cpu_backend.cpp:98-120; Backend::rope, backend.hpp:50-51).
+ * The position is *pos_dev when pos_dev is not NULL (read on the device, so a
+ * captured graph serves every token), else pos_host. A device position
+ * outside [0, table_rows) leaves data unchanged and sets device status 3. */
 HESA_CUDA_API int hesa_cuda_rope(float* data, int64_t n_heads, int64_t head_dim, const float* table,
-                                 const int32_t* pos_dev, int32_t pos_host, void* stream);
+                                 int32_t table_rows, const int32_t* pos_dev, int32_t pos_host, void* stream);
 
 /* Ring-buffer KV cache write: k_cache/v_cache [ctx, row_elems] fp16, slot
  * pos % ctx <- fp16(k), fp16(v) (round to nearest even). The KV cache of
- * the reference's design (docs/architecture.md:287-338). */
+ * the reference's design (docs/architecture.md:287-338). A negative device
+ * position writes nothing and sets device status 3. */
 HESA_CUDA_API int hesa_cuda_kv_store(const float* k, const float* v, void* k_cache, void* v_cache,
                                      int64_t row_elems, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
                                      void* stream);
@@ -188,8 +203,64 @@ HESA_CUDA_API int hesa_cuda_attention(const float* q, const void* k_cache, const
                                       const int32_t* pos_dev, int32_t pos_host, void* workspace,
                                       size_t workspace_bytes, void* stream);
 
-/* Sticky device-side status of the kernels' bounded waits: 0 when no wait
- * has ever timed out in this process, else a nonzero code naming the wait.
+/* ---------------------------------------------------------------------
+ * Decode step of a Llama-style decoder (the reference's layer loop over
+ * Backend ops: src/model, docs/architecture.md:287-338) on device tensors.
+ * ------------------------------------------------------------------- */
+
+typedef struct {
+    int32_t n_layer, d_model, n_head, n_kv_head, head_dim, d_ff, vocab;
+    int32_t ctx;        /* KV ring capacity (slots) */
+    float   rms_eps;    /* RMSNorm epsilon (Backend::rms_norm default 1e-6) */
+    float   rope_base;  /* unused by the step itself: the rope table carries it */
+    int32_t qtype;      /* type of every projection and the LM head */
+} hesa_cuda_model;
+
+/* Device pointers of one layer. Weights are packed GGUF rows [n_out, k];
+ * caches fp16 [ctx, n_kv_head * head_dim]. When wk starts right after the
+ * rows of wq and wv right after wk (and w_up right after w_gate), the step
+ * runs each group as one matvec. */
+typedef struct {
+    const void* wq;      /* [n_head * head_dim, d_model] */
+    const void* wk;      /* [n_kv_head * head_dim, d_model] */
+    const void* wv;
+    const void* wo;      /* [d_model, n_head * head_dim] */
+    const void* w_gate;  /* [d_ff, d_model] */
+    const void* w_up;
+    const void* w_down;  /* [d_model, d_ff] */
+    const float* attn_norm;  /* [d_model] */
+    const float* ffn_norm;
+    void* k_cache;
+    void* v_cache;
+} hesa_cuda_layer;
+
+/* Bytes of the decode step's workspace (intermediate vectors, attention and
+ * matvec scratch); zero-fill it once, every step leaves it reusable. */
+HESA_CUDA_API size_t hesa_cuda_decode_workspace_size(const hesa_cuda_model* model);
+
+/* x <- row *token_dev of the quantized embedding table [vocab, d_model],
+ * dequantized exactly. A token outside [0, vocab) leaves x unchanged and sets
+ * device status 3. */
+HESA_CUDA_API int hesa_cuda_embed(int qtype, const void* w_emb, int64_t vocab, int64_t d_model,
+                                  const int32_t* token_dev, float* x, void* stream);
+
+/* One token: logits [vocab] <- the decoder applied to the embedding x_embed
+ * [d_model] at position *pos_dev, writing K and V of every layer into slot
+ * pos % ctx of its caches and attending over min(pos + 1, ctx) slots.
+ *   layers: HOST array of n_layer structs (device pointers inside);
+ *   out_norm [d_model], w_out [vocab, d_model] packed rows;
+ *   rope_table: device copy of hesa_cuda_rope_table with rope_rows rows.
+ * Everything is enqueued on `stream` (capturable in a CUDA graph: the
+ * position and token are read on the device). */
+HESA_CUDA_API int hesa_cuda_decode_step(const hesa_cuda_model* model, const hesa_cuda_layer* layers,
+                                        const float* out_norm, const void* w_out, const float* rope_table,
+                                        int32_t rope_rows, const float* x_embed, const int32_t* pos_dev,
+                                        float* logits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Sticky device-side status of the kernels: 0 while nothing has gone wrong
+ * in this process, else the first code recorded: 1 a bulk copy did not land
+ * within the bounded wait, 2 a copy was still in flight when the kernel
+ * gave up, 3 a device-side position outside the KV cache or the rope table.
  * Reading synchronizes `stream`. hesa_cuda_clear_device_status resets it. */
 HESA_CUDA_API int hesa_cuda_device_status(void* stream, int* status_out);
 HESA_CUDA_API int hesa_cuda_clear_device_status(void* stream);

@@ -30,6 +30,19 @@ _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 
 
+class ModelCfg(ctypes.Structure):
+    """oracle_model_cfg (hesa_oracle.h)."""
+    _fields_ = [(n, _i64) for n in ("n_layer", "d_model", "n_head", "n_kv_head", "head_dim", "d_ff", "vocab",
+                                    "ctx")] + [("rms_eps", ctypes.c_float), ("rope_base", ctypes.c_float),
+                                               ("qtype", ctypes.c_int)]
+
+
+class LayerPtrs(ctypes.Structure):
+    """oracle_layer (hesa_oracle.h)."""
+    _fields_ = [(n, _vp) for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down", "attn_norm", "ffn_norm",
+                                   "k_cache", "v_cache")]
+
+
 def _p(a: np.ndarray, t=_vp):
     return ctypes.cast(a.ctypes.data, t)
 
@@ -55,6 +68,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_rope_table.argtypes = [_f32p, _f32p, ctypes.c_int32, _i64, ctypes.c_float]
         L.oracle_attention_f16kv.argtypes = [_f32p, _u16p, _u16p, _f32p, _i64, _i64, _i64,
                                              _i64, ctypes.c_int]
+        L.oracle_decode_step.argtypes = [ctypes.POINTER(ModelCfg), ctypes.POINTER(LayerPtrs), _f32p, _vp,
+                                         _f32p, ctypes.c_int32, _f32p, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -189,3 +204,29 @@ def attention_f16kv(q, k_cache, v_cache, n_head, n_kv_head, head_dim, n_ctx,
                                  _p(out, _f32p), n_head, n_kv_head, head_dim, n_ctx,
                                  n_threads or n_threads_default())
     return out
+
+
+def decode_step(cfg: dict, layers: list, out_norm: np.ndarray, w_out: np.ndarray, x_in: np.ndarray, pos: int,
+                n_threads: int | None = None) -> np.ndarray:
+    """oracle_decode_step: logits of one token. `layers` holds dicts of numpy
+    arrays (packed uint8 weights, fp32 norms, uint16 fp16 caches that are
+    updated in place)."""
+    c = ModelCfg(**{k: cfg[k] for k in ("n_layer", "d_model", "n_head", "n_kv_head", "head_dim", "d_ff", "vocab",
+                                         "ctx")}, rms_eps=cfg.get("rms_eps", 1e-6),
+                 rope_base=cfg.get("rope_base", 10000.0), qtype=cfg["qtype"])
+    arr = (LayerPtrs * len(layers))()
+    keep = []
+    for i, d in enumerate(layers):
+        for name, _ in LayerPtrs._fields_:
+            a = d[name]
+            assert a.flags["C_CONTIGUOUS"]
+            keep.append(a)
+            setattr(arr[i], name, a.ctypes.data)
+    logits = np.empty(cfg["vocab"], np.float32)
+    x = np.ascontiguousarray(x_in, np.float32)
+    on = np.ascontiguousarray(out_norm, np.float32)
+    rc = lib().oracle_decode_step(ctypes.byref(c), arr, _p(on, _f32p), w_out.ctypes.data, _p(x, _f32p),
+                                  int(pos), _p(logits, _f32p), n_threads or n_threads_default())
+    if rc:
+        raise RuntimeError("oracle_decode_step failed")
+    return logits

@@ -79,6 +79,14 @@ def test_dequantize_rejects_bad_arguments():
     assert L.hesa_cuda_dequantize(12, 0, 4, 256, FAKE, 256, None) == 2
 
 
+def test_quantize_rejects_bad_arguments():
+    L = H.lib()
+    assert L.hesa_cuda_quantize(5, FAKE, 4, 256, 256, FAKE, None) == 3
+    assert L.hesa_cuda_quantize(12, 0, 4, 256, 256, FAKE, None) == 2
+    assert L.hesa_cuda_quantize(12, FAKE, 4, 100, 100, FAKE, None) == 6
+    assert L.hesa_cuda_quantize(2, FAKE, 4, 64, 32, FAKE, None) == 6
+
+
 def test_error_type_carries_reference_code():
     with pytest.raises(H.HesaError) as ei:
         H._check(6)
