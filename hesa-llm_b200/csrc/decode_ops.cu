@@ -53,22 +53,37 @@ matmul_f32_kernel(const float* __restrict__ a, int n_out, int k, const float* __
     }
 }
 
-// One CTA per row.
-__global__ void __launch_bounds__(256)
+// One CTA of 1024 threads per row.
+__global__ void __launch_bounds__(1024)
 rms_norm_kernel(const float* __restrict__ in, const float* __restrict__ w, float* __restrict__ out, int n,
                 float eps) {
-    __shared__ float red[8];
+    // up to kRmsCache values per thread stay in registers between the two
+    // passes (every load of the row is issued before the reduction)
+    constexpr int kRmsCache = 8;
+    __shared__ float red[32];
     const float* row = in + static_cast<int64_t>(blockIdx.x) * n;
     float* o = out + static_cast<int64_t>(blockIdx.x) * n;
+    float v[kRmsCache];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
+#pragma unroll
+    for (int c = 0; c < kRmsCache; ++c) {
+        const int i = threadIdx.x + c * blockDim.x;
+        v[c] = i < n ? row[i] : 0.f;
+        ss = fmaf(v[c], v[c], ss);
+    }
+    for (int i = threadIdx.x + kRmsCache * blockDim.x; i < n; i += blockDim.x) ss = fmaf(row[i], row[i], ss);
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     float tot = 0.f;
     for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) tot += red[i];
     const float inv = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = row[i] * inv * w[i];
+#pragma unroll
+    for (int c = 0; c < kRmsCache; ++c) {
+        const int i = threadIdx.x + c * blockDim.x;
+        if (i < n) o[i] = v[c] * inv * w[i];
+    }
+    for (int i = threadIdx.x + kRmsCache * blockDim.x; i < n; i += blockDim.x) o[i] = row[i] * inv * w[i];
 }
 
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ o,
@@ -155,6 +170,36 @@ __global__ void kv_store_kernel(const float* __restrict__ k, const float* __rest
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnMaxDim = 256;
+constexpr int kAttnPos = 8;   // positions per warp step
+
+// DPL consecutive fp16 values (2, 4 or 8: one 4-, 8- or 16-byte load).
+template <int DPL> struct HalfVec;
+template <> struct HalfVec<2> {
+    uint32_t w;
+    __device__ float f(int i) const { return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> (16 * i)))); }
+};
+template <> struct HalfVec<4> {
+    uint2 w;
+    __device__ float f(int i) const {
+        const uint32_t x = i < 2 ? w.x : w.y;
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(x >> (16 * (i & 1)))));
+    }
+};
+template <> struct HalfVec<8> {
+    uint4 w;
+    __device__ float f(int i) const {
+        const uint32_t x = i < 2 ? w.x : i < 4 ? w.y : i < 6 ? w.z : w.w;
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(x >> (16 * (i & 1)))));
+    }
+};
+template <int DPL>
+__device__ __forceinline__ HalfVec<DPL> load_halves(const __half* p) {
+    HalfVec<DPL> v;
+    if constexpr (DPL == 2) v.w = *reinterpret_cast<const uint32_t*>(p);
+    else if constexpr (DPL == 4) v.w = *reinterpret_cast<const uint2*>(p);
+    else v.w = *reinterpret_cast<const uint4*>(p);
+    return v;
+}
 
 // grid (n_head, n_split); 4 warps; lane owns head_dim/32 consecutive dims.
 // Each CTA reduces its context chunk to (max, sum, acc[head_dim]) and writes
@@ -183,20 +228,50 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     float m = -INFINITY, l = 0.f, acc[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
-        const __half* kr = kc + j * row_stride + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
-        const __half* vr = vc + j * row_stride + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
-        float s = 0.f;
+    // kAttnPos positions per warp step: their K and V rows are loaded together
+    // (one vector load per lane and row), the score reductions interleave, and
+    // the running softmax is rescaled once per step
+    const __half* kbase = kc + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
+    const __half* vbase = vc + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
+    for (int jb = j0 + warp * kAttnPos; jb < j1; jb += kAttnWarps * kAttnPos) {
+        HalfVec<DPL> kv[kAttnPos], vv[kAttnPos];
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) s = fmaf(qv[i], __half2float(kr[i]), s);
-        s = warp_sum(s) * sc;
-        const float mn = fmaxf(m, s);
-        const float corr = expf(m - mn);   // 0 on the first position (m = -inf)
-        const float p = expf(s - mn);
-        l = l * corr + p;
+        for (int t = 0; t < kAttnPos; ++t) {
+            const int j = min(jb + t, j1 - 1);   // rows past the chunk repeat its last row (masked below)
+            kv[t] = load_halves<DPL>(kbase + j * row_stride);
+            vv[t] = load_halves<DPL>(vbase + j * row_stride);
+        }
+        float sco[kAttnPos];
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, __half2float(vr[i]), acc[i] * corr);
-        m = mn;
+        for (int t = 0; t < kAttnPos; ++t) {
+            float a = 0.f;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) a = fmaf(qv[i], kv[t].f(i), a);
+            sco[t] = a;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int t = 0; t < kAttnPos; ++t) sco[t] += __shfl_xor_sync(0xffffffffu, sco[t], o);
+        }
+        float mx = m;
+#pragma unroll
+        for (int t = 0; t < kAttnPos; ++t) {
+            sco[t] = jb + t < j1 ? sco[t] * sc : -INFINITY;
+            mx = fmaxf(mx, sco[t]);
+        }
+        const float corr = expf(m - mx);   // 0 on the first step (m = -inf)
+        l *= corr;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] *= corr;
+#pragma unroll
+        for (int t = 0; t < kAttnPos; ++t) {
+            const float p = expf(sco[t] - mx);   // 0 for a masked row
+            l += p;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, vv[t].f(i), acc[i]);
+        }
+        m = mx;
     }
 
     // combine the 4 warps of the CTA
@@ -281,7 +356,7 @@ cudaError_t matmul_f32(const float* a, int64_t n_out, int64_t k, const float* x,
 
 cudaError_t rms_norm(const float* in, const float* w, float* out, int64_t n_rows, int64_t n, float eps,
                      cudaStream_t s) {
-    rms_norm_kernel<<<static_cast<int>(n_rows), 256, 0, s>>>(in, w, out, static_cast<int>(n), eps);
+    rms_norm_kernel<<<static_cast<int>(n_rows), 1024, 0, s>>>(in, w, out, static_cast<int>(n), eps);
     return cudaGetLastError();
 }
 
@@ -329,8 +404,8 @@ size_t attention_workspace_bytes(int64_t n_head, int64_t head_dim, int64_t ctx) 
 }
 
 int attention_splits(int64_t ctx) {
-    // about 64 positions per warp-iteration group: 256 positions per CTA
-    int64_t n = (ctx + 255) / 256;
+    // 128 positions per CTA: 32 per warp, four 8-position steps
+    int64_t n = (ctx + 127) / 128;
     if (n < 1) n = 1;
     if (n > 64) n = 64;
     return static_cast<int>(n);
