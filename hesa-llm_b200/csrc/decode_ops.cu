@@ -153,6 +153,46 @@ __global__ void rope_kernel(float* __restrict__ data, int n_heads, int head_dim,
     }
 }
 
+// rope of q (in place) and of k, and the fp16 KV write of the rotated k and
+// of v into slot pos % ctx, in one kernel; same rounding as rope_kernel and
+// kv_store_kernel.
+__global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                               __half* __restrict__ kc, __half* __restrict__ vc, int n_head, int n_kv_head,
+                               int head_dim, const float* __restrict__ table, int table_rows, int ctx,
+                               const int32_t* __restrict__ pos_dev, int* __restrict__ status) {
+    const int32_t pos = *pos_dev;
+    if (pos < 0 || pos >= table_rows) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) record_status(status, kStatusBadPosition);
+        return;
+    }
+    const int half = head_dim >> 1;
+    const int64_t kd = static_cast<int64_t>(n_kv_head) * head_dim;
+    const int64_t slot = pos % ctx;
+    const float* cs = table + static_cast<int64_t>(pos) * head_dim;
+    const int n_pairs = (n_head + n_kv_head) * half;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_pairs + static_cast<int>(kd);
+         i += gridDim.x * blockDim.x) {
+        if (i < n_pairs) {
+            const int h = i / half, d = i - h * half;
+            const float c = cs[d], sn = cs[half + d];
+            if (h < n_head) {
+                float* row = q + static_cast<int64_t>(h) * head_dim;
+                const float x0 = row[d], x1 = row[d + half];
+                row[d] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+                row[d + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+            } else {
+                const int64_t off = static_cast<int64_t>(h - n_head) * head_dim;
+                const float x0 = k[off + d], x1 = k[off + d + half];
+                kc[slot * kd + off + d] = __float2half_rn(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+                kc[slot * kd + off + d + half] = __float2half_rn(__fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)));
+            }
+        } else {
+            const int64_t e = i - n_pairs;
+            vc[slot * kd + e] = __float2half_rn(v[e]);
+        }
+    }
+}
+
 __global__ void kv_store_kernel(const float* __restrict__ k, const float* __restrict__ v, __half* __restrict__ kc,
                                 __half* __restrict__ vc, int row_elems, int ctx, const int32_t* __restrict__ pos_dev,
                                 int32_t pos_host, int* __restrict__ status) {
@@ -394,6 +434,20 @@ cudaError_t kv_store(const float* k, const float* v, void* kc, void* vc, int64_t
                                                                   static_cast<__half*>(vc),
                                                                   static_cast<int>(row_elems),
                                                                   static_cast<int>(ctx), pos_dev, pos_host, status);
+    return cudaGetLastError();
+}
+
+cudaError_t rope_kv(float* q, const float* k, const float* v, void* kc, void* vc, int64_t n_head, int64_t n_kv_head,
+                    int64_t head_dim, const float* table, int32_t table_rows, int64_t ctx, const int32_t* pos_dev,
+                    cudaStream_t s) {
+    int* status = nullptr;
+    cudaError_t e = status_word(&status);
+    if (e != cudaSuccess) return e;
+    const int64_t n = (n_head + n_kv_head) * (head_dim / 2) + n_kv_head * head_dim;
+    rope_kv_kernel<<<grid_for(n, 256, 148 * 4), 256, 0, s>>>(
+        q, k, v, static_cast<__half*>(kc), static_cast<__half*>(vc), static_cast<int>(n_head),
+        static_cast<int>(n_kv_head), static_cast<int>(head_dim), table, table_rows, static_cast<int>(ctx), pos_dev,
+        status);
     return cudaGetLastError();
 }
 

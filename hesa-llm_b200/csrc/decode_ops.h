@@ -19,6 +19,10 @@ cudaError_t rope(float* data, int64_t n_heads, int64_t head_dim, const float* ta
                  const int32_t* pos_dev, int32_t pos_host, cudaStream_t s);
 cudaError_t kv_store(const float* k, const float* v, void* kc, void* vc, int64_t row_elems, int64_t ctx,
                      const int32_t* pos_dev, int32_t pos_host, cudaStream_t s);
+// rope(q) in place, rope(k), then k and v as fp16 into slot *pos_dev % ctx.
+cudaError_t rope_kv(float* q, const float* k, const float* v, void* kc, void* vc, int64_t n_head, int64_t n_kv_head,
+                    int64_t head_dim, const float* table, int32_t table_rows, int64_t ctx, const int32_t* pos_dev,
+                    cudaStream_t s);
 int attention_splits(int64_t ctx);
 size_t attention_workspace_bytes(int64_t n_head, int64_t head_dim, int64_t ctx);
 cudaError_t attention(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,

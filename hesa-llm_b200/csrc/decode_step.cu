@@ -11,12 +11,16 @@
 //
 // Q, K and V (and gate and up) run as ONE matvec when their packed rows lie
 // back to back in device memory (the upload can arrange that): the activation
-// is staged once and the outputs come out as one vector.
+// is staged once and the outputs come out as one vector. Where the row-strip
+// kernel takes the shape, the norms and SwiGLU are applied while it stages its
+// input and the residual adds happen in its epilogue, and rope and the KV
+// write are one kernel: six launches per layer.
 // The position (and the token of hesa_cuda_embed) is read from device memory
 // by every kernel that needs it, so a CUDA graph captured once replays for
 // every token.
 #include "../../include/hesa_cuda.h"
 #include "abi_errors.h"
+#include "decode_ops.h"
 #include "hesa_common.cuh"
 #include "qmatvec.h"
 #include "qtypes.cuh"
@@ -161,6 +165,16 @@ int hesa_cuda_decode_step(const hesa_cuda_model* m, const hesa_cuda_layer* layer
     auto mv = [&](const void* w, int64_t n_out, int64_t kk, const float* xin, float* yout) {
         return hesa_cuda_qmatvec(qt, w, n_out, kk, xin, kk, 1, yout, n_out, 1.0f, qmv_ws, L.qmv_bytes, stream);
     };
+    using hesa_cuda::StripInput;
+    auto fusable = [&](const void* w, int64_t n_out, int64_t kk, StripInput in) {
+        return hesa_cuda::qmv_strip_fused_eligible(qt, w, n_out, kk, in);
+    };
+    auto fmv = [&](const void* w, int64_t n_out, int64_t kk, const float* xin, StripInput in, const float* nw,
+                   float* yout, const float* resid) {
+        const cudaError_t e = hesa_cuda::qmv_strip_fused(qt, w, n_out, kk, xin, in, nw, m->rms_eps, yout, resid,
+                                                         1.0f, s);
+        return e == cudaSuccess ? HESA_CUDA_OK : hesa_cuda::record_cuda_error(e, "fused matvec");
+    };
     const cudaError_t ce = cudaMemcpyAsync(x, x_embed, D * 4, cudaMemcpyDeviceToDevice, s);
     int rc = ce == cudaSuccess ? HESA_CUDA_OK : hesa_cuda::record_cuda_error(ce, "copy of the embedding");
     for (int l = 0; l < m->n_layer && rc == HESA_CUDA_OK; ++l) {
@@ -172,34 +186,58 @@ int hesa_cuda_decode_step(const hesa_cuda_model* m, const hesa_cuda_layer* layer
         const bool qkv_joined = Ly.wk == wq + QD * rb_d && Ly.wv == wq + (QD + KD) * rb_d;
         const bool gu_joined = Ly.w_up == static_cast<const uint8_t*>(Ly.w_gate) + F * rb_d;
 
-        if (!rc) rc = hesa_cuda_rms_norm(x, Ly.attn_norm, h, 1, D, m->rms_eps, stream);
-        if (qkv_joined) {
-            if (!rc) rc = mv(Ly.wq, QD + 2 * KD, D, h, q);
+        // attention block: q|k|v = W (norm x) ; rope + KV write ; x += Wo attention(q)
+        if (qkv_joined && fusable(Ly.wq, QD + 2 * KD, D, StripInput::kRmsNorm)) {
+            if (!rc) rc = fmv(Ly.wq, QD + 2 * KD, D, x, StripInput::kRmsNorm, Ly.attn_norm, q, nullptr);
         } else {
-            if (!rc) rc = mv(Ly.wq, QD, D, h, q);
-            if (!rc) rc = mv(Ly.wk, KD, D, h, k);
-            if (!rc) rc = mv(Ly.wv, KD, D, h, v);
+            if (!rc) rc = hesa_cuda_rms_norm(x, Ly.attn_norm, h, 1, D, m->rms_eps, stream);
+            if (qkv_joined) {
+                if (!rc) rc = mv(Ly.wq, QD + 2 * KD, D, h, q);
+            } else {
+                if (!rc) rc = mv(Ly.wq, QD, D, h, q);
+                if (!rc) rc = mv(Ly.wk, KD, D, h, k);
+                if (!rc) rc = mv(Ly.wv, KD, D, h, v);
+            }
         }
-        if (!rc) rc = hesa_cuda_rope(q, NH, HD, rope_table, rope_rows, pos_dev, 0, stream);
-        if (!rc) rc = hesa_cuda_rope(k, NKV, HD, rope_table, rope_rows, pos_dev, 0, stream);
-        if (!rc) rc = hesa_cuda_kv_store(k, v, Ly.k_cache, Ly.v_cache, KD, m->ctx, pos_dev, 0, stream);
+        if (!rc) {
+            const cudaError_t e = hesa_cuda::rope_kv(q, k, v, Ly.k_cache, Ly.v_cache, NH, NKV, HD, rope_table,
+                                                     rope_rows, m->ctx, pos_dev, s);
+            if (e != cudaSuccess) rc = hesa_cuda::record_cuda_error(e, "rope + KV write");
+        }
         if (!rc) rc = hesa_cuda_attention(q, Ly.k_cache, Ly.v_cache, a, NH, NKV, HD, m->ctx, pos_dev, 0, att_ws,
                                           L.att_bytes, stream);
-        if (!rc) rc = mv(Ly.wo, D, QD, a, o);
-        if (!rc) rc = hesa_cuda_add(x, o, x, D, stream);
-        if (!rc) rc = hesa_cuda_rms_norm(x, Ly.ffn_norm, h, 1, D, m->rms_eps, stream);
-        if (gu_joined) {
-            if (!rc) rc = mv(Ly.w_gate, 2 * F, D, h, g);
+        if (fusable(Ly.wo, D, QD, StripInput::kPlain)) {
+            if (!rc) rc = fmv(Ly.wo, D, QD, a, StripInput::kPlain, nullptr, x, x);
         } else {
-            if (!rc) rc = mv(Ly.w_gate, F, D, h, g);
-            if (!rc) rc = mv(Ly.w_up, F, D, h, u);
+            if (!rc) rc = mv(Ly.wo, D, QD, a, o);
+            if (!rc) rc = hesa_cuda_add(x, o, x, D, stream);
         }
-        if (!rc) rc = hesa_cuda_silu_mul(g, u, g, F, stream);
-        if (!rc) rc = mv(Ly.w_down, D, F, g, o);
-        if (!rc) rc = hesa_cuda_add(x, o, x, D, stream);
+        // FFN block: g|u = W (norm x) ; x += Wdown (silu(g) * u)
+        if (gu_joined && fusable(Ly.w_gate, 2 * F, D, StripInput::kRmsNorm)) {
+            if (!rc) rc = fmv(Ly.w_gate, 2 * F, D, x, StripInput::kRmsNorm, Ly.ffn_norm, g, nullptr);
+        } else {
+            if (!rc) rc = hesa_cuda_rms_norm(x, Ly.ffn_norm, h, 1, D, m->rms_eps, stream);
+            if (gu_joined) {
+                if (!rc) rc = mv(Ly.w_gate, 2 * F, D, h, g);
+            } else {
+                if (!rc) rc = mv(Ly.w_gate, F, D, h, g);
+                if (!rc) rc = mv(Ly.w_up, F, D, h, u);
+            }
+        }
+        if (fusable(Ly.w_down, D, F, StripInput::kSiluMul)) {
+            if (!rc) rc = fmv(Ly.w_down, D, F, g, StripInput::kSiluMul, nullptr, x, x);   // g|u contiguous
+        } else {
+            if (!rc) rc = hesa_cuda_silu_mul(g, u, g, F, stream);
+            if (!rc) rc = mv(Ly.w_down, D, F, g, o);
+            if (!rc) rc = hesa_cuda_add(x, o, x, D, stream);
+        }
     }
-    if (!rc) rc = hesa_cuda_rms_norm(x, out_norm, h, 1, D, m->rms_eps, stream);
-    if (!rc) rc = mv(w_out, m->vocab, D, h, logits);
+    if (fusable(w_out, m->vocab, D, StripInput::kRmsNorm)) {
+        if (!rc) rc = fmv(w_out, m->vocab, D, x, StripInput::kRmsNorm, out_norm, logits, nullptr);
+    } else {
+        if (!rc) rc = hesa_cuda_rms_norm(x, out_norm, h, 1, D, m->rms_eps, stream);
+        if (!rc) rc = mv(w_out, m->vocab, D, h, logits);
+    }
     return rc;
 }
 

@@ -666,6 +666,29 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
 // ---------------------------------------------------------------------------
 
 constexpr int kStripMaxSlots = 16;
+constexpr int kStripBatch = 4;   // units of x one warp loads at a time
+
+// Input transforms of the strip kernel's staging (decode-step fusions).
+enum : int { kXPlain = 0, kXRmsNorm = 1, kXSiluMul = 2 };
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Positions 8*lane .. 8*lane+7 of unit u of a vector (zeros when u >= U).
+__device__ __forceinline__ void load8(const float* __restrict__ src, int u, int lane, int U, float (&v)[8]) {
+    if (u < U) {
+        const float4* p = reinterpret_cast<const float4*>(src + static_cast<size_t>(u) * 256 + lane * 8);
+        const float4 a = p[0], b = p[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    }
+}
 
 // Sum of v[0..3] over the 32 lanes of a warp in 6 shuffles: afterwards the
 // lanes with (lane & 7) == 0 hold the total of v[reduce4_row(lane)].
@@ -699,6 +722,7 @@ template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
 qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
                  float* __restrict__ y, float scale, int chunk_rows, int n_slots, int slot_stride, int rows_cap,
+                 int xmode, const float* __restrict__ norm_w, float eps, const float* __restrict__ resid,
                  int* __restrict__ status) {
     constexpr int UB = unit_bytes(QT);
     extern __shared__ __align__(128) uint8_t smem[];
@@ -735,6 +759,7 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         reinterpret_cast<uint8_t*>(part) + ((static_cast<size_t>(rows_cap) * wps * 4 + 15) & ~size_t(15)));
     int* done = reinterpret_cast<int*>(full + kStripMaxSlots);
     int* issued = done + kStripMaxSlots;
+    float* red = reinterpret_cast<float*>(issued + kStripMaxSlots);   // kWarps floats
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < n_slots; ++s) {
@@ -776,24 +801,57 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     grid_dep_wait();
 
     // x as digit planes, converted once per CTA (one warp per unit of 256;
-    // the loads of a batch of units are issued together)
-    constexpr int kBatch = 4;
-    for (int ub = warp; ub < U; ub += kWarps * kBatch) {
-        float v[kBatch][8];
+    // the loads of a batch of units are issued together). The input may be
+    // transformed on the way (decode-step fusions): RMSNorm, x * inv_rms * w
+    // with inv_rms = 1 / sqrt(mean(x^2) + eps) (every unit in one batch: the
+    // host keeps U <= kWarps * kStripBatch), or SwiGLU, silu(x[i]) * x[k + i].
+    if (xmode == kXRmsNorm) {
+        float v[kStripBatch][8];
+        float ss = 0.f;
 #pragma unroll
-        for (int jb = 0; jb < kBatch; ++jb) {
-            const int u = ub + jb * kWarps;
+        for (int jb = 0; jb < kStripBatch; ++jb) {
+            const int u = warp + jb * kWarps;
+            load8(x, u, lane, U, v[jb]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(v[jb][j], v[jb][j], ss);
+        }
+        ss = warp_sum_f(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w8 = 0; w8 < kWarps; ++w8) tot += red[w8];
+        const float inv = 1.0f / sqrtf(tot / static_cast<float>(k) + eps);
+#pragma unroll
+        for (int jb = 0; jb < kStripBatch; ++jb) {
+            const int u = warp + jb * kWarps;
             if (u < U) {
-                const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(u) * 256 + lane * 8);
-                const float4 va = xp[0], vb = xp[1];
-                v[jb][0] = va.x; v[jb][1] = va.y; v[jb][2] = va.z; v[jb][3] = va.w;
-                v[jb][4] = vb.x; v[jb][5] = vb.y; v[jb][6] = vb.z; v[jb][7] = vb.w;
+                float wn[8];
+                load8(norm_w, u, lane, U, wn);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[jb][j] = __fmul_rn(__fmul_rn(v[jb][j], inv), wn[j]);
+                stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
             }
         }
+    } else {
+        for (int ub = warp; ub < U; ub += kWarps * kStripBatch) {
+            float v[kStripBatch][8];
 #pragma unroll
-        for (int jb = 0; jb < kBatch; ++jb) {
-            const int u = ub + jb * kWarps;
-            if (u < U) stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
+            for (int jb = 0; jb < kStripBatch; ++jb) {
+                const int u = ub + jb * kWarps;
+                load8(x, u, lane, U, v[jb]);
+                if (xmode == kXSiluMul && u < U) {
+                    float up[8];
+                    load8(x + k, u, lane, U, up);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[jb][j] = (v[jb][j] / (1.0f + expf(-v[jb][j]))) * up[j];
+                }
+            }
+#pragma unroll
+            for (int jb = 0; jb < kStripBatch; ++jb) {
+                const int u = ub + jb * kWarps;
+                if (u < U) stage_unit<QT>(u, lane, v[jb], xplanes, xsums, xscale);
+            }
         }
     }
     if (threadIdx.x == 0)
@@ -866,7 +924,8 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
         float s = 0.f;
         for (int t = 0; t < wps; ++t) s += part[i * wps + t];
-        y[r0 + i] = s * scale;
+        const float val = s * scale;
+        y[r0 + i] = resid ? __fadd_rn(resid[r0 + i], val) : val;   // residual add, rounded as a separate add
     }
 }
 
@@ -987,7 +1046,7 @@ bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
     p.grid = static_cast<int>(grid);
     p.rows_cap = static_cast<int>((n_out + grid - 1) / grid);
     const size_t part_bytes = (static_cast<size_t>(p.rows_cap) * wps * 4 + 15) & ~size_t(15);
-    const size_t ctrl = kStripMaxSlots * (8 + 4 + 4);
+    const size_t ctrl = kStripMaxSlots * (8 + 4 + 4) + 64;   // + the RMSNorm reduction scratch
     const size_t fixed = x_region_bytes(U) + part_bytes + ctrl;
     if (fixed >= static_cast<size_t>(kMaxSmem)) return false;
     const size_t budget = kMaxSmem - fixed;
@@ -1018,7 +1077,8 @@ bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
 
 template <int QT>
 cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
-                         const StripPlan& p, cudaStream_t stream) {
+                         const StripPlan& p, int xmode, const float* norm_w, float eps, const float* resid,
+                         cudaStream_t stream) {
     static int smem_set[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1045,7 +1105,7 @@ cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, flo
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, qmv_strip_kernel<QT>, w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
-                              p.slot_stride, p.rows_cap, status);
+                              p.slot_stride, p.rows_cap, xmode, norm_w, eps, resid, status);
 }
 
 template <int QT>
@@ -1138,16 +1198,30 @@ bool qmv_strip_eligible(int qtype, const void* w, int64_t n_out, int64_t k) {
 
 cudaError_t qmv_strip(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y, float scale,
                       cudaStream_t stream) {
+    return qmv_strip_fused(qtype, w, n_out, k, x, StripInput::kPlain, nullptr, 0.f, y, nullptr, scale, stream);
+}
+
+bool qmv_strip_fused_eligible(int qtype, const void* w, int64_t n_out, int64_t k, StripInput in) {
+    if (!qmv_strip_eligible(qtype, w, n_out, k)) return false;
+    return in != StripInput::kRmsNorm || k <= static_cast<int64_t>(kWarps) * kStripBatch * 256;
+}
+
+cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, StripInput in,
+                            const float* norm_w, float eps, float* y, const float* resid, float scale,
+                            cudaStream_t stream) {
     StripPlan p;
     if (!plan_strip(qtype, n_out, k, p)) return cudaErrorInvalidValue;
+    if (in == StripInput::kRmsNorm && (!norm_w || k > static_cast<int64_t>(kWarps) * kStripBatch * 256))
+        return cudaErrorInvalidValue;
+    const int xm = in == StripInput::kRmsNorm ? kXRmsNorm : in == StripInput::kSiluMul ? kXSiluMul : kXPlain;
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_out), kk = static_cast<int>(k);
     switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, stream);
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, stream);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -31,6 +31,16 @@ bool qmv_strip_eligible(int qtype, const void* w, int64_t n_out, int64_t k);
 cudaError_t qmv_strip(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y, float scale,
                       cudaStream_t stream);
 
+// The strip kernel with a transformed input and an optional residual add, for
+// the decode step: y = resid + scale * W . f(x) with f = identity, RMSNorm
+// (x * inv_rms * norm_w, inv_rms = 1/sqrt(mean(x^2) + eps); k <= 12288) or
+// SwiGLU (silu(x[i]) * x[k + i]; x holds 2k values). resid may equal y.
+enum class StripInput { kPlain, kRmsNorm, kSiluMul };
+bool qmv_strip_fused_eligible(int qtype, const void* w, int64_t n_out, int64_t k, StripInput in);
+cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, StripInput in,
+                            const float* norm_w, float eps, float* y, const float* resid, float scale,
+                            cudaStream_t stream);
+
 // One warp per row, any k that is a multiple of the block size.
 cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,
                         int64_t batch, float* y, int64_t ldy, float scale, cudaStream_t stream);
