@@ -39,6 +39,9 @@ import time
 
 import numpy as np
 
+# NCCL's informational lines go to stdout, which carries the one JSON line
+os.environ.setdefault("NCCL_DEBUG", "WARN")
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "hesa-llm_b200")
 for _p in (ROOT, PKG):
