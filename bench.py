@@ -361,6 +361,29 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None):
                 kv_bytes=d["kv_bytes"])
 
 
+def profile_decode(steps: int):
+    """A few eager decode steps of a 2-layer model with the 7B shapes (per-layer
+    launches as in the full model, small enough for an ncu launch list)."""
+    import torch
+    import hesa_cuda as H
+    cfg = dict(DECODE_7B, n_layer=2)
+    dev = torch.device("cuda", 0)
+    d = build_decoder(cfg, dev, seed=5)
+    x = torch.empty(cfg["d_model"], dtype=torch.float32, device=dev)
+    logits = torch.empty(cfg["vocab"], dtype=torch.float32, device=dev)
+    pos = torch.tensor([DECODE_POS], dtype=torch.int32, device=dev)
+    tok = torch.tensor([3], dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(max(steps, 1)):
+            H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok, out=x, stream=stream)
+            H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos, logits, d["ws"],
+                          stream=stream)
+        stream.synchronize()
+    log(f"profile decode done: {steps} step(s), logits finite: {bool(torch.isfinite(logits).all())}")
+    return 0
+
+
 # --------------------------------------------------------------------------
 # GPU arm
 # --------------------------------------------------------------------------
@@ -644,6 +667,9 @@ def main():
     ap.add_argument("--impl", default="hesa", choices=["hesa", "reference"])
     ap.add_argument("--profile", action="store_true",
                     help="untimed: build inputs, run --steps plain steps, exit (for ncu captures)")
+    ap.add_argument("--profile-decode", action="store_true",
+                    help="untimed: a 2-layer model of the 7B decode shapes, --steps eager decode steps "
+                         "(for ncu launch lists of one step)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus else 1)))
@@ -652,6 +678,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.profile_decode:
+        return profile_decode(args.steps)
     return run_gpu(args, rank, world, local_rank)
 
 

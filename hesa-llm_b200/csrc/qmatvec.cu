@@ -841,10 +841,13 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
                 const int u = ub + jb * kWarps;
                 load8(x, u, lane, U, v[jb]);
                 if (xmode == kXSiluMul && u < U) {
+                    // the value is rounded to 22 bits below its unit's maximum right
+                    // after, so the fast exp and divide (a few ulp) change nothing
+                    // that survives that rounding
                     float up[8];
                     load8(x + k, u, lane, U, up);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) v[jb][j] = (v[jb][j] / (1.0f + expf(-v[jb][j]))) * up[j];
+                    for (int j = 0; j < 8; ++j) v[jb][j] = __fdividef(v[jb][j], 1.0f + __expf(-v[jb][j])) * up[j];
                 }
             }
 #pragma unroll
