@@ -6,7 +6,10 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstring>
+#include <vector>
 
 namespace hesa {
 
@@ -41,6 +44,19 @@ Result<T> fail_as(Error e) {
     return std::unexpected{make_error_code(e)};
 }
 
+// true when v is F32 and laid out row-major without gaps (the CPU backend's
+// element-wise kernels read data() as a flat array)
+bool contiguous_f32(const TensorView& v) {
+    if (v.dtype() != Dtype::F32 || v.data() == nullptr) return false;
+    const auto st = v.byte_strides();
+    size_t expect = sizeof(float);
+    for (size_t d = v.ndim(); d-- > 0;) {
+        if (v.shape()[d] > 1 && st[d] != expect) return false;
+        expect *= static_cast<size_t>(v.shape()[d]);
+    }
+    return true;
+}
+
 float load_f32(const TensorView& v, int64_t i, int64_t j) {
     const auto st = v.byte_strides();
     const auto* base = static_cast<const uint8_t*>(v.data());
@@ -70,6 +86,8 @@ CudaBackend::~CudaBackend() {
     for (auto& kv : weights_) cudaFree(kv.second.ptr);
     for (DevBuf* b : {&d_x_, &d_y_, &d_ws_})
         if (b->ptr) cudaFree(b->ptr);
+    for (DevBuf& b : scratch_)
+        if (b.ptr) cudaFree(b.ptr);
     for (DevBuf* b : {&h_x_, &h_y_})
         if (b->ptr) cudaFreeHost(b->ptr);
     if (stream_) cudaStreamDestroy(static_cast<cudaStream_t>(stream_));
@@ -89,7 +107,9 @@ size_t CudaBackend::device_memory() const {
 }
 
 size_t CudaBackend::device_memory_used() const {
-    return weight_bytes_ + d_x_.bytes + d_y_.bytes + d_ws_.bytes;
+    size_t n = weight_bytes_ + d_x_.bytes + d_y_.bytes + d_ws_.bytes;
+    for (const DevBuf& b : scratch_) n += b.bytes;
+    return n;
 }
 
 Result<void> CudaBackend::ensure(DevBuf& b, size_t bytes) {
@@ -212,22 +232,194 @@ Result<void> CudaBackend::matmul(TensorView a, TensorView b, TensorView out, flo
     return ok();
 }
 
-Result<void> CudaBackend::add(TensorView, TensorView, TensorView) { return error(Error::BACKEND_NOT_AVAILABLE); }
-Result<void> CudaBackend::mul(TensorView, TensorView, TensorView) { return error(Error::BACKEND_NOT_AVAILABLE); }
-Result<void> CudaBackend::softmax(TensorView, TensorView, int) { return error(Error::BACKEND_NOT_AVAILABLE); }
-Result<void> CudaBackend::rms_norm(TensorView, TensorView, TensorView, float) {
-    return error(Error::BACKEND_NOT_AVAILABLE);
-}
-Result<void> CudaBackend::rope(TensorView, std::span<const int32_t>, float, int) {
-    return error(Error::BACKEND_NOT_AVAILABLE);
-}
-Result<void> CudaBackend::silu(TensorView, TensorView) { return error(Error::BACKEND_NOT_AVAILABLE); }
-Result<void> CudaBackend::scaled_dot_product_attention(TensorView, TensorView, TensorView, TensorView, TensorView,
-                                                       float) {
-    return error(Error::BACKEND_NOT_AVAILABLE);
+Result<float*> CudaBackend::upload(const TensorView& v, int slot) {
+    if (!contiguous_f32(v)) return fail_as<float*>(Error::INVALID_ARGUMENT);
+    const size_t bytes = static_cast<size_t>(v.nelements()) * sizeof(float);
+    auto r = ensure(scratch_[slot], bytes > 0 ? bytes : sizeof(float));
+    if (!r) return std::unexpected{r.error()};
+    if (bytes && cudaMemcpyAsync(scratch_[slot].ptr, v.data(), bytes, cudaMemcpyHostToDevice,
+                                 static_cast<cudaStream_t>(stream_)) != cudaSuccess)
+        return fail_as<float*>(Error::CUDA_ERROR);
+    return static_cast<float*>(scratch_[slot].ptr);
 }
 
-Result<Tensor> CudaBackend::quantize(TensorView, Dtype) { return fail_as<Tensor>(Error::BACKEND_NOT_AVAILABLE); }
+Result<void> CudaBackend::download(int slot, TensorView& v) {
+    if (!contiguous_f32(v)) return error(Error::INVALID_ARGUMENT);
+    const size_t bytes = static_cast<size_t>(v.nelements()) * sizeof(float);
+    cudaStream_t s = static_cast<cudaStream_t>(stream_);
+    if (bytes) HESA_CHECK(from_cuda(cudaMemcpyAsync(v.data(), scratch_[slot].ptr, bytes, cudaMemcpyDeviceToHost, s)));
+    return from_cuda(cudaStreamSynchronize(s));
+}
+
+Result<void> CudaBackend::add(TensorView a, TensorView b, TensorView out) {
+    HESA_CHECK(activate());
+    if (a.nelements() != b.nelements() || a.nelements() != out.nelements()) return error(Error::SHAPE_MISMATCH);
+    if (a.nelements() == 0) return ok();
+    auto da = upload(a, 0);
+    if (!da) return std::unexpected{da.error()};
+    auto db = upload(b, 1);
+    if (!db) return std::unexpected{db.error()};
+    HESA_CHECK(from_abi(hesa_cuda_add(*da, *db, *da, a.nelements(), stream_)));
+    return download(0, out);
+}
+
+Result<void> CudaBackend::mul(TensorView a, TensorView b, TensorView out) {
+    HESA_CHECK(activate());
+    if (a.nelements() != b.nelements() || a.nelements() != out.nelements()) return error(Error::SHAPE_MISMATCH);
+    if (a.nelements() == 0) return ok();
+    auto da = upload(a, 0);
+    if (!da) return std::unexpected{da.error()};
+    auto db = upload(b, 1);
+    if (!db) return std::unexpected{db.error()};
+    HESA_CHECK(from_abi(hesa_cuda_mul(*da, *db, *da, a.nelements(), stream_)));
+    return download(0, out);
+}
+
+Result<void> CudaBackend::silu(TensorView in, TensorView out) {
+    HESA_CHECK(activate());
+    if (in.nelements() != out.nelements()) return error(Error::SHAPE_MISMATCH);
+    if (in.nelements() == 0) return ok();
+    auto d = upload(in, 0);
+    if (!d) return std::unexpected{d.error()};
+    HESA_CHECK(from_abi(hesa_cuda_silu_mul(*d, nullptr, *d, in.nelements(), stream_)));
+    return download(0, out);
+}
+
+Result<void> CudaBackend::softmax(TensorView in, TensorView out, int axis) {
+    HESA_CHECK(activate());
+    if (in.ndim() == 0 || in.nelements() != out.nelements()) return error(Error::SHAPE_MISMATCH);
+    if (axis != -1 && axis != static_cast<int>(in.ndim()) - 1) return error(Error::BACKEND_NOT_AVAILABLE);
+    if (in.nelements() == 0) return ok();
+    const int64_t n = in.shape()[in.ndim() - 1];
+    auto d = upload(in, 0);
+    if (!d) return std::unexpected{d.error()};
+    HESA_CHECK(from_abi(hesa_cuda_softmax(*d, *d, in.nelements() / n, n, stream_)));
+    return download(0, out);
+}
+
+Result<void> CudaBackend::rms_norm(TensorView in, TensorView weight, TensorView out, float eps) {
+    HESA_CHECK(activate());
+    if (in.ndim() == 0 || in.nelements() != out.nelements()) return error(Error::SHAPE_MISMATCH);
+    const int64_t n = in.shape()[in.ndim() - 1];
+    if (static_cast<int64_t>(weight.nelements()) != n) return error(Error::SHAPE_MISMATCH);
+    if (in.nelements() == 0) return ok();
+    auto d = upload(in, 0);
+    if (!d) return std::unexpected{d.error()};
+    auto dw = upload(weight, 1);
+    if (!dw) return std::unexpected{dw.error()};
+    auto r = ensure(scratch_[2], static_cast<size_t>(in.nelements()) * sizeof(float));
+    if (!r) return r;
+    HESA_CHECK(from_abi(hesa_cuda_rms_norm(*d, *dw, static_cast<float*>(scratch_[2].ptr), in.nelements() / n, n,
+                                           eps, stream_)));
+    return download(2, out);
+}
+
+Result<void> CudaBackend::rope(TensorView in_out, std::span<const int32_t> positions, float freq_base, int n_dims) {
+    HESA_CHECK(activate());
+    if (in_out.ndim() < 3 || n_dims <= 0 || (n_dims & 1) || in_out.shape()[2] != n_dims)
+        return error(Error::SHAPE_MISMATCH);
+    const int64_t n_tokens = in_out.shape()[0], n_heads = in_out.shape()[1];
+    if (!positions.empty() && static_cast<int64_t>(positions.size()) < n_tokens) return error(Error::SHAPE_MISMATCH);
+    int32_t max_pos = 0;
+    for (int64_t t = 0; t < n_tokens; ++t) {
+        const int32_t p = positions.empty() ? static_cast<int32_t>(t) : positions[t];
+        if (p < 0) return error(Error::INVALID_ARGUMENT);
+        max_pos = std::max(max_pos, p);
+    }
+    // angle table rows 0 .. max_pos, with the CPU backend's own float formulas
+    std::vector<float> table(static_cast<size_t>(max_pos + 1) * n_dims);
+    HESA_CHECK(from_abi(hesa_cuda_rope_table(table.data(), max_pos + 1, n_dims, freq_base)));
+    auto r = ensure(scratch_[3], table.size() * sizeof(float));
+    if (!r) return r;
+    cudaStream_t s = static_cast<cudaStream_t>(stream_);
+    HESA_CHECK(from_cuda(cudaMemcpyAsync(scratch_[3].ptr, table.data(), table.size() * sizeof(float),
+                                         cudaMemcpyHostToDevice, s)));
+    auto d = upload(in_out, 0);
+    if (!d) return std::unexpected{d.error()};
+    for (int64_t t = 0; t < n_tokens; ++t) {
+        const int32_t p = positions.empty() ? static_cast<int32_t>(t) : positions[t];
+        HESA_CHECK(from_abi(hesa_cuda_rope(*d + t * n_heads * n_dims, n_heads, n_dims,
+                                           static_cast<const float*>(scratch_[3].ptr), max_pos + 1, nullptr, p,
+                                           stream_)));
+    }
+    return download(0, in_out);   // waits, so `table` outlives the copy
+}
+
+Result<void> CudaBackend::scaled_dot_product_attention(TensorView q, TensorView k, TensorView v, TensorView out,
+                                                       TensorView mask, float scale) {
+    HESA_CHECK(activate());
+    if (mask.data() != nullptr) return error(Error::BACKEND_NOT_AVAILABLE);   // the CPU backend ignores it too
+    if (q.ndim() != 3 || k.ndim() != 3 || v.ndim() != 3 || out.ndim() != 3) return error(Error::SHAPE_MISMATCH);
+    const int64_t n_q = q.shape()[0], n_heads = q.shape()[1], d = q.shape()[2], n_k = k.shape()[0];
+    if (k.shape()[1] != n_heads || k.shape()[2] != d || v.shape()[0] != n_k || v.shape()[1] != n_heads ||
+        v.shape()[2] != d || out.shape()[0] != n_q || out.shape()[1] != n_heads || out.shape()[2] != d)
+        return error(Error::SHAPE_MISMATCH);
+    if (!contiguous_f32(q) || !contiguous_f32(k) || !contiguous_f32(v) || !contiguous_f32(out))
+        return error(Error::INVALID_ARGUMENT);
+    const float sc = scale > 0.0f ? scale : 1.0f / std::sqrt(static_cast<float>(d));
+    // per head: scores = sc * Q_h K_h^T (matmul with a = K_h [n_k, d]),
+    // softmax over keys, out_h = P V_h (matmul with a = V_h^T [d, n_k])
+    const float* hq = static_cast<const float*>(q.data());
+    const float* hk = static_cast<const float*>(k.data());
+    const float* hv = static_cast<const float*>(v.data());
+    float* ho = static_cast<float*>(out.data());
+    std::vector<float> qh(static_cast<size_t>(n_q) * d), kh(static_cast<size_t>(n_k) * d),
+        vt(static_cast<size_t>(d) * n_k), oh(static_cast<size_t>(n_q) * d);
+    const size_t bq = qh.size() * 4, bk = kh.size() * 4, bs = static_cast<size_t>(n_q) * n_k * 4;
+    for (int slot : {0, 1, 2, 4})
+        if (auto r = ensure(scratch_[slot], slot == 0 ? bq : slot == 1 ? bk : slot == 2 ? bs : bq); !r) return r;
+    if (auto r = ensure(scratch_[5], bk); !r) return r;
+    cudaStream_t s = static_cast<cudaStream_t>(stream_);
+    float* dq = static_cast<float*>(scratch_[0].ptr);
+    float* dk = static_cast<float*>(scratch_[1].ptr);
+    float* ds = static_cast<float*>(scratch_[2].ptr);
+    float* dout = static_cast<float*>(scratch_[4].ptr);
+    float* dvt = static_cast<float*>(scratch_[5].ptr);
+    for (int64_t h = 0; h < n_heads; ++h) {
+        for (int64_t i = 0; i < n_q; ++i)
+            std::memcpy(&qh[i * d], hq + (i * n_heads + h) * d, d * 4);
+        for (int64_t j = 0; j < n_k; ++j) {
+            std::memcpy(&kh[j * d], hk + (j * n_heads + h) * d, d * 4);
+            for (int64_t e = 0; e < d; ++e) vt[e * n_k + j] = hv[(j * n_heads + h) * d + e];
+        }
+        HESA_CHECK(from_cuda(cudaMemcpyAsync(dq, qh.data(), bq, cudaMemcpyHostToDevice, s)));
+        HESA_CHECK(from_cuda(cudaMemcpyAsync(dk, kh.data(), bk, cudaMemcpyHostToDevice, s)));
+        HESA_CHECK(from_cuda(cudaMemcpyAsync(dvt, vt.data(), bk, cudaMemcpyHostToDevice, s)));
+        HESA_CHECK(from_abi(hesa_cuda_matmul_f32(dk, n_k, d, dq, d, n_q, ds, n_k, sc, stream_)));
+        HESA_CHECK(from_abi(hesa_cuda_softmax(ds, ds, n_q, n_k, stream_)));
+        HESA_CHECK(from_abi(hesa_cuda_matmul_f32(dvt, d, n_k, ds, n_k, n_q, dout, d, 1.0f, stream_)));
+        HESA_CHECK(from_cuda(cudaMemcpyAsync(oh.data(), dout, bq, cudaMemcpyDeviceToHost, s)));
+        HESA_CHECK(from_cuda(cudaStreamSynchronize(s)));   // host staging is reused by the next head
+        for (int64_t i = 0; i < n_q; ++i) std::memcpy(ho + (i * n_heads + h) * d, &oh[i * d], d * 4);
+    }
+    return ok();
+}
+
+Result<Tensor> CudaBackend::quantize(TensorView src, Dtype target_dtype) {
+    auto a = activate();
+    if (!a) return std::unexpected{a.error()};
+    const int qt = qtype_of(target_dtype);
+    if (qt <= 0) return fail_as<Tensor>(Error::BACKEND_NOT_AVAILABLE);
+    if (src.ndim() != 2 || !contiguous_f32(src)) return fail_as<Tensor>(Error::INVALID_ARGUMENT);
+    const int64_t rows = src.shape()[0], k = src.shape()[1];
+    const size_t rb = hesa_cuda_row_bytes(qt, k);
+    if (rb == 0) return fail_as<Tensor>(Error::SHAPE_MISMATCH);
+    auto d = upload(src, 0);
+    if (!d) return std::unexpected{d.error()};
+    if (auto r = ensure(scratch_[1], rb * rows); !r) return std::unexpected{r.error()};
+    if (const int rc = hesa_cuda_quantize(qt, *d, rows, k, k, scratch_[1].ptr, stream_); rc != 0)
+        return fail_as<Tensor>(static_cast<Error>(rc));
+    // a quantized Tensor holds one byte per element (dtype_size 1), more than
+    // the packed rows need; the rows go at its start, as Model::load puts them
+    const int64_t shape[2] = {rows, k};
+    Tensor t(target_dtype, std::span<const int64_t>(shape, 2), this);
+    if (t.nbytes() < rb * rows) return fail_as<Tensor>(Error::INTERNAL_ERROR);
+    cudaStream_t s = static_cast<cudaStream_t>(stream_);
+    if (cudaMemcpyAsync(t.data(), scratch_[1].ptr, rb * rows, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return fail_as<Tensor>(Error::CUDA_ERROR);
+    return std::move(t);
+}
 
 Result<void> CudaBackend::synchronize() {
     HESA_CHECK(activate());

@@ -45,6 +45,13 @@ public:
     // out = scale * a @ b with a = W [n_out, k] (Q4_0/Q8_0/Q4_K/Q5_K/Q6_K or
     // F32), b = [k, batch] F32 (any byte strides, e.g. a transposed [batch, k]
     // view), out = [n_out, batch] F32 (any byte strides).
+    // The other ops follow the CPU backend (src/backend/cpu_backend.cpp:162-294)
+    // on contiguous F32 views: add, mul, silu element-wise; softmax and
+    // rms_norm over rows of the last dimension; rope on [n_tokens, n_heads,
+    // n_dims] with one position per token (rotate-half); attention on
+    // q [n_q, heads, d], k, v [n_k, heads, d], no mask, scale 1/sqrt(d) unless
+    // given. Unlike the CPU backend, attention overwrites `out` (the CPU
+    // version adds to whatever it holds).
     Result<void> matmul(TensorView a, TensorView b, TensorView out, float scale = 1.0f) override;
     Result<void> add(TensorView a, TensorView b, TensorView out) override;
     Result<void> mul(TensorView a, TensorView b, TensorView out) override;
@@ -73,6 +80,10 @@ private:
     Result<void> ensure_host(DevBuf& b, size_t bytes);
     Result<const void*> device_weights(const void* host, size_t bytes);
     Result<void> activate() const;
+    // contiguous F32 view -> device scratch buffer `slot` (returns the device pointer)
+    Result<float*> upload(const TensorView& v, int slot);
+    // device scratch buffer `slot` -> contiguous F32 view, then synchronize
+    Result<void> download(int slot, TensorView& v);
 
     int device_ = 0;
     size_t memory_limit_ = 0;
@@ -80,6 +91,7 @@ private:
     std::map<std::pair<const void*, size_t>, DevBuf> weights_;
     size_t weight_bytes_ = 0;
     DevBuf d_x_, d_y_, d_ws_, h_x_, h_y_;
+    DevBuf scratch_[6];   // device operands of the element-wise and attention ops
     size_t ws_zeroed_ = 0;
 };
 

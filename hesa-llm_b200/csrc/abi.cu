@@ -236,6 +236,9 @@ int hesa_cuda_attention(const float* q, const void* k_cache, const void* v_cache
                         int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
                         void* workspace, size_t workspace_bytes, void* stream) {
     if (!q || !k_cache || !v_cache || !out || !workspace) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (!aligned16(k_cache) || !aligned16(v_cache))
+        return fail(HESA_CUDA_INVALID_ARGUMENT, "KV caches must be 16-byte aligned");
+    if (ctx > 131072) return fail(HESA_CUDA_SHAPE_MISMATCH, "ctx above 131072 slots");
     if (n_head <= 0 || n_kv_head <= 0 || n_head % n_kv_head != 0 || ctx <= 0 || (!pos_dev && pos_host < 0))
         return fail(HESA_CUDA_SHAPE_MISMATCH, "bad shape");
     if (head_dim != 64 && head_dim != 128 && head_dim != 256)

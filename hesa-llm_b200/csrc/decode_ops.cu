@@ -211,6 +211,9 @@ __global__ void kv_store_kernel(const float* __restrict__ k, const float* __rest
 constexpr int kAttnWarps = 4;
 constexpr int kAttnMaxDim = 256;
 constexpr int kAttnPos = 8;   // positions per warp step
+constexpr int kAttnMaxSplits = 1024;
+constexpr int kAttnStage = 32;   // positions per pipeline stage: kAttnWarps warps x kAttnPos
+static_assert(kAttnStage == kAttnWarps * kAttnPos, "a stage is one step of every warp");
 
 // DPL consecutive fp16 values (2, 4 or 8: one 4-, 8- or 16-byte load).
 template <int DPL> struct HalfVec;
@@ -232,6 +235,17 @@ template <> struct HalfVec<8> {
         return __half2float(__ushort_as_half(static_cast<unsigned short>(x >> (16 * (i & 1)))));
     }
 };
+// 16-byte global -> shared copy that completes asynchronously (cp.async);
+// cp_async_wait_all waits for this thread's copies.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                 ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// wait until at most one committed group of this thread is still in flight
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 template <int DPL>
 __device__ __forceinline__ HalfVec<DPL> load_halves(const __half* p) {
     HalfVec<DPL> v;
@@ -268,51 +282,84 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     float m = -INFINITY, l = 0.f, acc[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-    // kAttnPos positions per warp step: their K and V rows are loaded together
-    // (one vector load per lane and row), the score reductions interleave, and
-    // the running softmax is rescaled once per step
-    const __half* kbase = kc + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
-    const __half* vbase = vc + static_cast<int64_t>(kvh) * head_dim + lane * DPL;
-    for (int jb = j0 + warp * kAttnPos; jb < j1; jb += kAttnWarps * kAttnPos) {
-        HalfVec<DPL> kv[kAttnPos], vv[kAttnPos];
-#pragma unroll
-        for (int t = 0; t < kAttnPos; ++t) {
-            const int j = min(jb + t, j1 - 1);   // rows past the chunk repeat its last row (masked below)
-            kv[t] = load_halves<DPL>(kbase + j * row_stride);
-            vv[t] = load_halves<DPL>(vbase + j * row_stride);
+
+    // The chunk streams through shared memory in stages of kAttnStage
+    // positions, two buffers deep: the cp.async copies of stage s + 2 are in
+    // flight while stage s is computed (16-byte pieces, every thread issuing
+    // its share). Each warp takes kAttnPos positions of every stage: the score
+    // reductions interleave and the running softmax is rescaled once per step.
+    extern __shared__ __align__(16) uint8_t attn_smem[];
+    __half* sbuf = reinterpret_cast<__half*>(attn_smem);   // [2][K|V][kAttnStage][head_dim]
+    constexpr int kPieces = DPL * 32 * 2 / 16;               // 16-byte pieces per row
+    const int rows = j1 > j0 ? j1 - j0 : 0;
+    const int n_stage = (rows + kAttnStage - 1) / kAttnStage;
+    const __half* kg = kc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
+    const __half* vg = vc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
+    auto issue = [&](int st) {
+        if (st < n_stage) {
+            __half* sk = sbuf + static_cast<int64_t>(st & 1) * 2 * kAttnStage * head_dim;
+            __half* sv = sk + kAttnStage * head_dim;
+            const int r0 = st * kAttnStage, nr = min(kAttnStage, rows - r0);
+            for (int c = threadIdx.x; c < nr * kPieces; c += blockDim.x) {
+                const int r = c / kPieces, o = (c - r * kPieces) * 8;
+                cp_async16(sk + r * head_dim + o, kg + static_cast<int64_t>(r0 + r) * row_stride + o);
+                cp_async16(sv + r * head_dim + o, vg + static_cast<int64_t>(r0 + r) * row_stride + o);
+            }
         }
-        float sco[kAttnPos];
+        cp_async_commit();   // an empty group when there is no such stage
+    };
+    issue(0);
+    issue(1);
+    for (int st = 0; st < n_stage; ++st) {
+        cp_async_wait_one();   // stage st has landed (stage st + 1 may still be in flight)
+        __syncthreads();
+        const __half* sk = sbuf + static_cast<int64_t>(st & 1) * 2 * kAttnStage * head_dim;
+        const __half* sv = sk + kAttnStage * head_dim;
+        const int jb = j0 + st * kAttnStage + warp * kAttnPos;   // this warp's first position
+        if (jb < j1) {
+            HalfVec<DPL> kv[kAttnPos], vv[kAttnPos];
 #pragma unroll
-        for (int t = 0; t < kAttnPos; ++t) {
-            float a = 0.f;
+            for (int t = 0; t < kAttnPos; ++t) {
+                const int j = min(jb + t, j1 - 1) - (j0 + st * kAttnStage);   // past the chunk: repeat, masked
+                kv[t] = load_halves<DPL>(sk + j * head_dim + lane * DPL);
+                vv[t] = load_halves<DPL>(sv + j * head_dim + lane * DPL);
+            }
+            float sco[kAttnPos];
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) a = fmaf(qv[i], kv[t].f(i), a);
-            sco[t] = a;
+            for (int t = 0; t < kAttnPos; ++t) {
+                float a = 0.f;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) a = fmaf(qv[i], kv[t].f(i), a);
+                sco[t] = a;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int t = 0; t < kAttnPos; ++t) sco[t] += __shfl_xor_sync(0xffffffffu, sco[t], o);
+            }
+            float mx = m;
+#pragma unroll
+            for (int t = 0; t < kAttnPos; ++t) {
+                sco[t] = jb + t < j1 ? sco[t] * sc : -INFINITY;
+                mx = fmaxf(mx, sco[t]);
+            }
+            const float corr = expf(m - mx);   // 0 on the first step (m = -inf)
+            l *= corr;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) acc[i] *= corr;
+#pragma unroll
+            for (int t = 0; t < kAttnPos; ++t) {
+                const float p = expf(sco[t] - mx);   // 0 for a masked row
+                l += p;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, vv[t].f(i), acc[i]);
+            }
+            m = mx;
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int t = 0; t < kAttnPos; ++t) sco[t] += __shfl_xor_sync(0xffffffffu, sco[t], o);
-        }
-        float mx = m;
-#pragma unroll
-        for (int t = 0; t < kAttnPos; ++t) {
-            sco[t] = jb + t < j1 ? sco[t] * sc : -INFINITY;
-            mx = fmaxf(mx, sco[t]);
-        }
-        const float corr = expf(m - mx);   // 0 on the first step (m = -inf)
-        l *= corr;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] *= corr;
-#pragma unroll
-        for (int t = 0; t < kAttnPos; ++t) {
-            const float p = expf(sco[t] - mx);   // 0 for a masked row
-            l += p;
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, vv[t].f(i), acc[i]);
-        }
-        m = mx;
+        __syncthreads();   // every warp is done with this buffer before it is refilled
+        issue(st + 2);
     }
+    cp_async_wait_all();   // nothing left in flight (the trailing groups are empty)
 
     // combine the 4 warps of the CTA
     __shared__ float s_m[kAttnWarps], s_l[kAttnWarps];
@@ -354,11 +401,16 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
         if (last) {
             cuda::atomic_thread_fence(cuda::memory_order_acquire, cuda::thread_scope_device);
             const float* base = part + static_cast<int64_t>(h) * n_split * (head_dim + 2);
+            // split maxima read by all lanes at once; the weighted sum walks the
+            // splits in order, eight loads in flight at a time
             float MM = -INFINITY;
-            for (int s2 = 0; s2 < n_split; ++s2) MM = fmaxf(MM, base[s2 * (head_dim + 2)]);
+            for (int s2 = lane; s2 < n_split; s2 += 32) MM = fmaxf(MM, base[s2 * (head_dim + 2)]);
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) MM = fmaxf(MM, __shfl_xor_sync(0xffffffffu, MM, o2));
             float LL = 0.f, o[DPL];
 #pragma unroll
             for (int i = 0; i < DPL; ++i) o[i] = 0.f;
+#pragma unroll 8
             for (int s2 = 0; s2 < n_split; ++s2) {
                 const float* p = base + s2 * (head_dim + 2);
                 const float f = p[0] == -INFINITY ? 0.f : expf(p[0] - MM);
@@ -458,11 +510,33 @@ size_t attention_workspace_bytes(int64_t n_head, int64_t head_dim, int64_t ctx) 
 }
 
 int attention_splits(int64_t ctx) {
-    // 128 positions per CTA: 32 per warp, four 8-position steps
+    // 128 positions per CTA: four 32-position stages
     int64_t n = (ctx + 127) / 128;
     if (n < 1) n = 1;
-    if (n > 64) n = 64;
+    if (n > kAttnMaxSplits) n = kAttnMaxSplits;
     return static_cast<int>(n);
+}
+
+template <int DPL>
+cudaError_t launch_attention(dim3 grid, size_t smem, cudaStream_t s, const float* q, const __half* k, const __half* v,
+                             float* out, int nh, int nkv, int c, const int32_t* pos_dev, int32_t pos_host, int chunk,
+                             float* part, int* counters) {
+    if (smem > 48 * 1024) {
+        static int set[64] = {0};
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+        if (set[dev] < static_cast<int>(smem)) {
+            e = cudaFuncSetAttribute(attention_kernel<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            set[dev] = static_cast<int>(smem);
+        }
+    }
+    attention_kernel<DPL><<<grid, kAttnWarps * 32, smem, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk,
+                                                               part, counters);
+    return cudaGetLastError();
 }
 
 cudaError_t attention(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,
@@ -477,13 +551,16 @@ cudaError_t attention(const float* q, const void* kc, const void* vc, float* out
     const __half* k = static_cast<const __half*>(kc);
     const __half* v = static_cast<const __half*>(vc);
     const int nh = static_cast<int>(n_head), nkv = static_cast<int>(n_kv_head), c = static_cast<int>(ctx);
+    // two stage buffers of K and V
+    const size_t smem = static_cast<size_t>(2 * kAttnStage) * static_cast<size_t>(head_dim) * 2 * 2;
+    cudaError_t e = cudaSuccess;
     switch (head_dim) {
-        case 64: attention_kernel<2><<<grid, kAttnWarps * 32, 0, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
-        case 128: attention_kernel<4><<<grid, kAttnWarps * 32, 0, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
-        case 256: attention_kernel<8><<<grid, kAttnWarps * 32, 0, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
+        case 64: e = launch_attention<2>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
+        case 128: e = launch_attention<4>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
+        case 256: e = launch_attention<8>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
+    return e;
 }
 
 }  // namespace hesa_cuda

@@ -195,7 +195,7 @@ HESA_CUDA_API size_t hesa_cuda_attention_workspace_size(int64_t n_head, int64_t 
 /* Single-query attention over min(pos+1, ctx) slots of the fp16 ring:
  * out[h] = softmax(q[h] . K / sqrt(head_dim)) V with kv head
  * h / (n_head / n_kv_head). q, out: [n_head, head_dim] fp32; head_dim 64,
- * 128 or 256. The SDPA of CPU_Backend (cpu_backend.cpp:225-294) extended to
+ * 128 or 256; caches 16-byte aligned, ctx <= 131072 slots. The SDPA of CPU_Backend (cpu_backend.cpp:225-294) extended to
  * GQA and the fp16 cache; Backend::scaled_dot_product_attention
  * (backend.hpp:55-57). */
 HESA_CUDA_API int hesa_cuda_attention(const float* q, const void* k_cache, const void* v_cache, float* out,
