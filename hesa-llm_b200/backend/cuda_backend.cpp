@@ -404,13 +404,17 @@ Result<Tensor> CudaBackend::quantize(TensorView src, Dtype target_dtype) {
     const int64_t rows = src.shape()[0], k = src.shape()[1];
     const size_t rb = hesa_cuda_row_bytes(qt, k);
     if (rb == 0) return fail_as<Tensor>(Error::SHAPE_MISMATCH);
+    // a quantized Tensor holds one byte per element (dtype_size 1,
+    // src/tensor/tensor.cpp:28-37): enough for the packed rows of every type
+    // but Q8_0, whose 34-byte blocks of 32 need 17/16 bytes per element (the
+    // reference loader truncates Q8_0 rows to that size, gguf_loader.cpp:305-309)
+    if (rb * static_cast<size_t>(rows) > static_cast<size_t>(rows * k)) return fail_as<Tensor>(Error::INVALID_FORMAT);
     auto d = upload(src, 0);
     if (!d) return std::unexpected{d.error()};
     if (auto r = ensure(scratch_[1], rb * rows); !r) return std::unexpected{r.error()};
     if (const int rc = hesa_cuda_quantize(qt, *d, rows, k, k, scratch_[1].ptr, stream_); rc != 0)
         return fail_as<Tensor>(static_cast<Error>(rc));
-    // a quantized Tensor holds one byte per element (dtype_size 1), more than
-    // the packed rows need; the rows go at its start, as Model::load puts them
+    // the packed rows go at the start of the Tensor, as Model::load puts them
     const int64_t shape[2] = {rows, k};
     Tensor t(target_dtype, std::span<const int64_t>(shape, 2), this);
     if (t.nbytes() < rb * rows) return fail_as<Tensor>(Error::INTERNAL_ERROR);

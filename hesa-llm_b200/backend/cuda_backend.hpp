@@ -51,7 +51,9 @@ public:
     // n_dims] with one position per token (rotate-half); attention on
     // q [n_q, heads, d], k, v [n_k, heads, d], no mask, scale 1/sqrt(d) unless
     // given. Unlike the CPU backend, attention overwrites `out` (the CPU
-    // version adds to whatever it holds).
+    // version adds to whatever it holds). quantize packs [rows, k] F32 into
+    // Q4_0/Q4_K/Q5_K/Q6_K rows; Q8_0 is INVALID_FORMAT because its packed rows
+    // do not fit a Tensor of one byte per element.
     Result<void> matmul(TensorView a, TensorView b, TensorView out, float scale = 1.0f) override;
     Result<void> add(TensorView a, TensorView b, TensorView out) override;
     Result<void> mul(TensorView a, TensorView b, TensorView out) override;
