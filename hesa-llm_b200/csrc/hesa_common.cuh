@@ -65,6 +65,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
+// 2-D tiled tensor copy (TMA) of the box at element coordinates (x, y) of the
+// tensor map into shared memory, completing on `bar`. No cluster multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tensor_map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst_smem)), "l"(tensor_map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Named barrier `id` (1..15) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_barrier(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

@@ -35,6 +35,7 @@
 #include "hesa_common.cuh"
 #include "qtypes.cuh"
 #include "qmatvec.h"
+#include "xdigits.cuh"
 
 #include <cuda/atomic>
 
@@ -139,11 +140,6 @@ __device__ __forceinline__ void dot3u(uint32_t q, const XQuarter& xq, int w, int
     p[2] = dp4a_us(q, xq.d[2][w], p[2]);
 }
 
-// 65536*a2 + 256*a1 + a0 in fp32.
-__device__ __forceinline__ float combine3(int a0, int a1, int a2) {
-    return fmaf(static_cast<float>(a2), 65536.f, fmaf(static_cast<float>(a1), 256.f, static_cast<float>(a0)));
-}
-
 // sum_k x_k over group g of the quarter (fp32), from the digit sums.
 __device__ __forceinline__ float xsum(const XQuarter& xq, int g) {
     return xq.s * combine3(xq.ds[g][0], xq.ds[g][1], xq.ds[g][2]);
@@ -154,18 +150,6 @@ __device__ __forceinline__ float xsum(const XQuarter& xq, int g) {
 // the unit in shared memory.
 template <int QT>
 __device__ __forceinline__ float unit_dot(const uint8_t* u, int c, const XQuarter& xq);
-
-// K-quant scale/min pairs of sub-blocks 2c, 2c+1 (byte 0, byte 1 of each).
-__device__ __forceinline__ void kq_pairs(const uint4& h, int c, uint32_t& sc2, uint32_t& m2) {
-    const uint32_t s = 16u * (c & 1);
-    if (c >> 1) {
-        sc2 = ((h.w >> s) & 0x0F0Fu) | ((h.y >> (s + 2)) & 0x3030u);
-        m2 = ((h.w >> (s + 4)) & 0x0F0Fu) | ((h.z >> (s + 2)) & 0x3030u);
-    } else {
-        sc2 = (h.y >> s) & 0x3F3Fu;
-        m2 = (h.z >> s) & 0x3F3Fu;
-    }
-}
 
 template <>
 __device__ __forceinline__ float unit_dot<kQ4_K>(const uint8_t* u, int c, const XQuarter& xq) {
@@ -324,45 +308,12 @@ __device__ __forceinline__ int64_t owner_warp(int64_t c, int64_t C, int64_t W) {
 }
 
 // Convert one unit (256 activations) to digit planes in shared memory; lane
-// L holds positions 8L..8L+7 in v.
-//
-// The balanced digits of X (|X| < 2^22) are the bytes of X + 0x808080, each
-// minus 128: adding 1.5 * 2^23 to x / s in one fused multiply-add rounds it to
-// the integer X (nearest, ties to even, as rint) in the low mantissa bits, so
-// X + 0x808080 is that float's bit pattern minus (0x4B400000 - 0x808080).
-// PRMT gathers byte p of four such words into digit-plane word p, and XOR
-// 0x80 per byte turns the biased bytes into signed digits.
+// L holds positions 8L..8L+7 in v (digits as unit_digits makes them).
 template <int QT>
 __device__ __forceinline__ void stage_unit(int unit, int lane, const float (&v)[8], uint8_t* xplanes, uint8_t* xsums,
                                            float* xscale) {
-    // largest magnitude: max.NaN keeps a NaN, inf compares above every finite
-    // value, and the bit patterns of non-negative floats order as integers
-    float fm = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) fm = fmax_nan(fm, fabsf(v[j]));
-    const uint32_t am = __reduce_max_sync(0xffffffffu, __float_as_uint(fm));
-    // a non-finite activation makes the unit's scale NaN, so every output it
-    // touches is NaN, as the fp32 reference sum would be inf or NaN
-    const bool finite = am < 0x7F800000u;
-    // exponent E of the largest magnitude: |x| < 2^(E+1); s = 2^(E-21)
-    int E = static_cast<int>(am >> 23) - 127;
-    if (E < -100) E = -100;  // activations below 2^-100 round to zero
-    const float inv_s = __uint_as_float(static_cast<uint32_t>(21 - E + 127) << 23);
-    const float s = finite ? __uint_as_float(static_cast<uint32_t>(E - 21 + 127) << 23) : __int_as_float(0x7FC00000);
-    // (digits of a non-finite unit are meaningless; its scale is NaN)
-    uint32_t Y[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) Y[j] = __float_as_uint(fmaf(v[j], inv_s, 12582912.0f)) - 0x4ABF7F80u;
     uint32_t dw[3][2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint32_t* y = Y + 4 * h;
-        const uint32_t t01 = prmt(y[0], y[1], 0x5140u), t23 = prmt(y[2], y[3], 0x5140u);
-        const uint32_t u01 = prmt(y[0], y[1], 0x0062u), u23 = prmt(y[2], y[3], 0x0062u);
-        dw[0][h] = prmt(t01, t23, 0x5410u) ^ 0x80808080u;
-        dw[1][h] = prmt(t01, t23, 0x7632u) ^ 0x80808080u;
-        dw[2][h] = prmt(u01, u23, 0x5410u) ^ 0x80808080u;
-    }
+    const float s = unit_digits(v, dw);
     int c, i0;
     unit_pos_to_slot<QT>(lane * 8, c, i0);
     uint8_t* qbase = xplanes + static_cast<size_t>(unit * 4 + c) * kQPlaneStride;

@@ -40,6 +40,20 @@ __device__ __forceinline__ void kq_scale_min(const uint8_t* s, int j, int& sc, i
     }
 }
 
+// K-quant scale/min pairs of sub-blocks 2c, 2c+1 (byte 0, byte 1 of each),
+// from the first 16 bytes of a Q4_K/Q5_K block (h.x = d, dmin; h.y..h.w = the
+// 12-byte scale field); the packing of kq_scale_min, two sub-blocks at once.
+__device__ __forceinline__ void kq_pairs(const uint4& h, int c, uint32_t& sc2, uint32_t& m2) {
+    const uint32_t s = 16u * (c & 1);
+    if (c >> 1) {
+        sc2 = ((h.w >> s) & 0x0F0Fu) | ((h.y >> (s + 2)) & 0x3030u);
+        m2 = ((h.w >> (s + 4)) & 0x0F0Fu) | ((h.z >> (s + 2)) & 0x3030u);
+    } else {
+        sc2 = (h.y >> s) & 0x3F3Fu;
+        m2 = (h.z >> s) & 0x3F3Fu;
+    }
+}
+
 // Exact value of weight `i` (0 <= i < block_elems) of the block at `b`.
 template <int QT>
 __device__ __forceinline__ float deq_weight(const uint8_t* b, int i) {

@@ -64,10 +64,11 @@ HESA_CUDA_API const char* hesa_cuda_version(void);
 HESA_CUDA_API size_t hesa_cuda_row_bytes(int qtype, int64_t k);
 
 /* Device workspace the matvec needs for n_out x k at this batch, in bytes
- * (cross-warp partial sums and arrival counters). The workspace must be
- * zero-filled once before its first use; every successful call leaves it
- * zero-filled again, so it can be reused by later calls on the same stream.
- * After a call that reports HESA_CUDA_ERROR, zero it again. */
+ * (arrival counters, cross-CTA partial sums and, for batch >= 2, the staged
+ * activations). The workspace must be zero-filled once before its first use;
+ * every successful call leaves its counters at zero again, so it can be
+ * reused by later calls on the same stream, at any batch up to the one it was
+ * sized for. After a call that reports HESA_CUDA_ERROR, zero it again. */
 HESA_CUDA_API size_t hesa_cuda_qmatvec_workspace_size(int qtype, int64_t n_out, int64_t k, int64_t batch);
 
 /* y[b*ldy + n] = scale * sum_k deq(W[n,k]) * x[b*ldx + k]
@@ -77,12 +78,15 @@ HESA_CUDA_API size_t hesa_cuda_qmatvec_workspace_size(int qtype, int64_t n_out, 
  * TensorView b, TensorView out, float scale) (include/hesa/backend.hpp:43-44)
  * whose CPU semantics are cpu_matmul_f32 (src/backend/cpu_backend.cpp:24-41):
  * a = W [n_out, k], b = x^T [k, batch], out = y^T [n_out, batch].
- * Each batch column is one streaming pass over W on CUDA cores.
+ * Batch 1 is one streaming pass over W on CUDA cores. Q4_K and Q5_K with
+ * batch >= 2 (k a multiple of 256) run on the tensor cores, reading W once
+ * per 16 activation rows; the other types make one pass per batch column.
  * x and y must be 16-byte aligned with ldx, ldy multiples of 4.
- * The workspace is used only by the split-row kernel (rows longer than 24576
- * weights, or matrices too tall for one strip of rows per SM); a call that
- * needs it and gets less than hesa_cuda_qmatvec_workspace_size bytes fails
- * with HESA_CUDA_INVALID_ARGUMENT before launching anything.
+ * The workspace is used by the batched kernel and the split-row kernel (rows
+ * longer than 24576 weights, or matrices too tall for one strip of rows per
+ * SM); a call that needs it and gets less than
+ * hesa_cuda_qmatvec_workspace_size bytes fails with
+ * HESA_CUDA_INVALID_ARGUMENT before launching anything.
  * Consecutive calls on one stream overlap (programmatic dependent launch):
  * a call starts fetching W while the previous kernel on the stream finishes,
  * and reads x only after that kernel has completed. W must therefore not be

@@ -46,6 +46,19 @@ def test_workspace_size_is_small_and_positive():
     assert H.workspace_bytes(3, 16, 256) == 0
 
 
+def test_batched_workspace_holds_staged_activations():
+    # Q4_K / Q5_K at batch >= 2 stage the activations' digit planes in the
+    # workspace: 12 KB per unit of 256 (16 rows), 6 KB for up to 8 rows
+    one = H.workspace_bytes(12, 4096, 11008, 1)
+    b8 = H.workspace_bytes(12, 4096, 11008, 8)
+    b16 = H.workspace_bytes(12, 4096, 11008, 16)
+    assert one < b8 < b16
+    assert b16 >= 43 * 12 * 1024
+    assert H.workspace_bytes(12, 4096, 11008, 64) == b16      # 16 rows per launch pair
+    # types without the batched kernel keep the batch-1 size
+    assert H.workspace_bytes(8, 4096, 11008, 16) == H.workspace_bytes(8, 4096, 11008, 1)
+
+
 FAKE = 1 << 20  # non-null, 16-byte aligned, never dereferenced: validation fails first
 
 
@@ -66,6 +79,9 @@ def call(qt=12, w=FAKE, n=64, k=256, x=FAKE, ldx=256, b=1, y=FAKE, ldy=64, ws=FA
     # k = 32768 takes the split-row kernel, the one that needs the workspace
     (dict(k=32768, ldx=32768, wsb=16), 2),   # workspace too small
     (dict(k=32768, ldx=32768, ws=0), 2),
+    # Q4_K at batch >= 2 takes the batched kernel, which needs the workspace
+    (dict(b=4, wsb=16), 2),
+    (dict(b=4, ws=FAKE + 8), 2),
 ])
 def test_qmatvec_rejects_bad_arguments_without_launching(kwargs, code):
     assert call(**kwargs) == code
