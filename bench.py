@@ -317,6 +317,56 @@ def build_decoder(cfg, dev, seed):
                 ws=H.decode_workspace(m, dev), bytes_token=bytes_token, weight_bytes=wbytes, kv_bytes=kv_bytes)
 
 
+BATCHED_SHAPES = ((4096, 11008), (11008, 4096))
+BATCHED_B = (1, 4, 8, 16)
+
+
+def run_batched(dev, stream, reps: int = 20):
+    """Batched-decode matvec: Q4_K [n_out x k] against B activation rows, for
+    the two FFN shapes of the 7B model and B in BATCHED_B. Eight weight copies
+    (203 MB, more than L2) rotate inside one CUDA graph; device-timed.
+    Returns {shape: {B: (us per matvec, algorithmic GB/s)}}, bytes = W + 4 B (k + n_out)."""
+    import torch
+    import hesa_cuda as H
+    qt, nw = QT["Q4_K"], 8
+    out = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    for (n, k) in BATCHED_SHAPES:
+        w0 = H.quantize(qt, torch.randn((n, k), generator=g, device=dev) * 0.02)
+        ws_list = [w0.clone() for _ in range(nw)]
+        del w0
+        res = {}
+        for B in BATCHED_B:
+            x = torch.randn((B, k), generator=g, device=dev)
+            y = torch.empty((B, n), device=dev)
+            wsp = H.make_workspace(qt, n, k, B, device=dev)
+            with torch.cuda.stream(stream):
+                for w in ws_list:
+                    H.qmatvec(qt, w, x, y=y, workspace=wsp, stream=stream)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for w in ws_list:
+                        H.qmatvec(qt, w, x, y=y, workspace=wsp, stream=stream)
+                for _ in range(3):
+                    graph.replay()
+                stream.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+                e1.synchronize()
+            us = e0.elapsed_time(e1) * 1000.0 / (reps * nw)
+            byts = n * row_bytes(qt, k) + 4 * B * (k + n)
+            res[B] = (round(us, 2), round(byts / us / 1e3, 1))
+            del graph
+        out[f"{n}x{k}"] = res
+        del ws_list
+    return out
+
+
 def run_decode(dev, stream, steps: int, warmup: int, pg=None):
     """tokens/s of the 7B-shaped Q4_K decode step (embedding lookup + every
     layer + LM head), one CUDA graph per token, device-timed."""
@@ -593,6 +643,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     # the 7B-shaped Q4_K decode step, one full replica per rank
     dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg)
+    batched = run_batched(dev, stream) if rank == 0 else None
 
     # max over ranks
     times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec["ms"]], dtype=torch.float64, device=dev)
@@ -647,6 +698,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                        "timing": "embedding lookup + 32 layers + LM head captured as one CUDA graph per token, "
                                  "replayed between CUDA events",
                        "logits_finite": dec["finite"]},
+            "batched": {"workload": "Q4_K [n_out x k] times B activation rows (batched decode), "
+                                    "one launch per 16 rows on the tensor cores (B >= 2)",
+                        "us_and_gbs": batched,
+                        "timing": "8 rotating weight copies (203 MB > L2) in one CUDA graph, CUDA events, rank 0"},
             "clocks": clocks,
             "cpu_baseline": cpu_base,
         }

@@ -17,4 +17,11 @@ size_t qmm_workspace_bytes(int qtype, int64_t n_out, int64_t k, int64_t batch);
 cudaError_t qmm(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
                 float* y, int64_t ldy, float scale, void* workspace, cudaStream_t stream);
 
+// The same on the 5th-generation tensor cores (tcgen05 / TMEM / TMA,
+// qmm_tc.cu): one launch per 16 activation rows.
+bool qmm_tc_eligible(int qtype, const void* w, int64_t n_out, int64_t k, int64_t batch);
+size_t qmm_tc_workspace_bytes(int qtype, int64_t n_out, int64_t k, int64_t batch);
+cudaError_t qmm_tc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
+                   float* y, int64_t ldy, float scale, void* workspace, cudaStream_t stream);
+
 }  // namespace hesa_cuda
