@@ -19,9 +19,10 @@
 //   * the activations' digit planes (3 x rows, padded to N = 32 or 48 "column
 //     planes") sit in shared memory in the canonical K-major core-matrix
 //     layout (8 rows x 16 bytes per core matrix);
-//   * one thread issues 16 tcgen05.mma kind::i8 (u8 x s8 -> s32, M = 128,
-//     K = 32: eight k-steps for each half) with A from TMEM, B from shared
-//     memory, the two accumulators in TMEM, and commits them to an mbarrier;
+//   * one thread of its own warp issues 16 tcgen05.mma kind::i8 (u8 x s8 ->
+//     s32, M = 128, K = 32: eight k-steps for each half) with A from TMEM, B
+//     from shared memory, the two accumulators in TMEM, and commits them to
+//     an mbarrier;
 //   * the row threads read the accumulators back (tcgen05.ld) and apply the
 //     unit's scales.
 // A and the accumulators are double-buffered in TMEM, so a unit's unpacking,
@@ -53,7 +54,7 @@ namespace {
 
 constexpr int kRows = 128;                          // weight rows per tile = TMEM lanes
 constexpr int kRowWarps = 8;                        // two per TMEM lane quarter
-constexpr int kThreads = (kRowWarps + 1) * 32;      // + the producer warp
+constexpr int kThreads = (kRowWarps + 2) * 32;      // + the producer warp and the MMA warp
 constexpr int kSU = 2;                              // units per weight copy
 constexpr int kWSlots = 3;
 constexpr int kPlanSms = 148;
@@ -252,6 +253,39 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap wmap2, const __grid_constant__
         }
         return;
     }
+    if (warp == kRowWarps + 1) {
+        // ---- MMA warp: one thread issues every unit's MMAs once its operand is in TMEM ----
+        if (lane == 0) {
+            int q = 0;
+            for (int it = i0; it < i1 && !*abort_v; ++it) {
+                const int s = it / RT;
+                const int nu = (s + 1) * U / S - s * U / S;
+                for (int ui = 0; ui < nu; ++ui, ++q) {
+                    bool go = mbar_wait_bounded(&aready[q & 1], static_cast<uint32_t>(q >> 1) & 1u, status,
+                                                kStatusWaitTimeout);
+                    if (go && q >= 2)
+                        go = mbar_wait_bounded(&dfree[q & 1], static_cast<uint32_t>((q >> 1) - 1) & 1u, status,
+                                               kStatusWaitTimeout);
+                    if (!go || *abort_v) {
+                        *abort_v = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = tmem + static_cast<uint32_t>(128 * (q & 1));
+                    const uint32_t d = tmem + 256u + static_cast<uint32_t>(2 * N * (q & 1));
+                    const uint32_t xb = smem_addr(sx + static_cast<size_t>(ui) * XUB);
+#pragma unroll
+                    for (int st = 0; st < 8; ++st) {
+                        const uint64_t bd = umma_desc(xb + st * KSTEP, (N / 8) * 128, 128);
+                        tc_mma_ts(d, a + 8 * st, bd, IDESC, st > 0);
+                        tc_mma_ts(d + N, a + 64 + 8 * st, bd, IDESC, st > 0);
+                    }
+                    tc_commit(&dready[q & 1]);
+                }
+            }
+        }
+        return;
+    }
 
     // ---- row warps ----
     const int wq = warp & 3, hf = warp >> 2;
@@ -342,29 +376,6 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap wmap2, const __grid_constant__
                 if (lane == 0) {
                     mbar_arrive(&aready[q & 1]);
                     if ((ui & 1) == 1 || ui == nu - 1) mbar_arrive(&wfree[slot]);   // the copy is consumed
-                }
-                // ---- one thread issues the unit's MMAs ----
-                if (warp == 0 && lane == 0 && !*abort_v) {
-                    bool go = mbar_wait_bounded(&aready[q & 1], static_cast<uint32_t>(q >> 1) & 1u, status,
-                                                kStatusWaitTimeout);
-                    if (go && q >= 2)
-                        go = mbar_wait_bounded(&dfree[q & 1], static_cast<uint32_t>((q >> 1) - 1) & 1u, status,
-                                               kStatusWaitTimeout);
-                    if (go) {
-                        tc_fence_after();
-                        const uint32_t a = tmem + static_cast<uint32_t>(128 * (q & 1));
-                        const uint32_t d = tmem + 256u + static_cast<uint32_t>(2 * N * (q & 1));
-                        const uint32_t xb = smem_addr(sx + static_cast<size_t>(ui) * XUB);
-#pragma unroll
-                        for (int st = 0; st < 8; ++st) {
-                            const uint64_t bd = umma_desc(xb + st * KSTEP, (N / 8) * 128, 128);
-                            tc_mma_ts(d, a + 8 * st, bd, IDESC, st > 0);
-                            tc_mma_ts(d + N, a + 64 + 8 * st, bd, IDESC, st > 0);
-                        }
-                        tc_commit(&dready[q & 1]);
-                    } else {
-                        *abort_v = 1;
-                    }
                 }
                 __syncwarp();
             }
