@@ -255,16 +255,26 @@ __device__ __forceinline__ HalfVec<DPL> load_halves(const __half* p) {
     return v;
 }
 
-// grid (n_head, n_split); 4 warps; lane owns head_dim/32 consecutive dims.
-// Each CTA reduces its context chunk to (max, sum, acc[head_dim]) and writes
-// it to the workspace; the last CTA of the head (ticket) combines the splits
-// in split order and writes out.
+// grid (n_head, n_split); 4 warps; 128 positions per CTA. Each CTA reduces
+// its context chunk to (max, sum, acc[head_dim]) and writes it to the
+// workspace; the last CTA of the head (ticket) combines the splits in split
+// order and writes out.
+//
+// A warp step takes 8 positions. Scores: lanes 4t .. 4t+3 score position t,
+// lane (t, qq) taking the 16-byte pieces qq, qq+4, ... of the K row (a
+// quarter-warp reads 64 contiguous bytes of two rows 16 bytes out of bank
+// phase: K rows are padded by 16 bytes) against the matching pieces of q held
+// in registers; two shuffles combine the four partial dots. The step's
+// maximum and sum run over the lanes 4 apart (three shuffles each), one
+// exponential per lane. P . V: lane owns head_dim/32 consecutive dims.
 template <int DPL>  // dims per lane (head_dim / 32)
 __global__ void __launch_bounds__(kAttnWarps * 32)
 attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
                  float* __restrict__ out, int n_head, int n_kv_head, int ctx, const int32_t* __restrict__ pos_dev,
                  int32_t pos_host, int chunk, float* __restrict__ part, int* __restrict__ counters) {
     const int head_dim = DPL * 32;
+    constexpr int HD = DPL * 32, KS = HD + 8;   // K rows in halves, padded by 16 bytes
+    constexpr int QP = HD / 8 / 4;              // 16-byte pieces of q per lane
     const int h = blockIdx.x, split = blockIdx.y, n_split = gridDim.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int32_t pos = pos_dev ? *pos_dev : pos_host;
@@ -273,9 +283,12 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     const int64_t row_stride = static_cast<int64_t>(n_kv_head) * head_dim;
     const float sc = 1.0f / sqrtf(static_cast<float>(head_dim));
 
-    float qv[DPL];
+    const int t8 = lane >> 2, qq = lane & 3;   // scoring: position t8 of the step, piece phase qq
+    float qv[QP][8];
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) qv[i] = q[static_cast<int64_t>(h) * head_dim + lane * DPL + i];
+    for (int c = 0; c < QP; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qv[c][i] = q[static_cast<int64_t>(h) * HD + 8 * (4 * c + qq) + i];
 
     const int j0 = split * chunk;
     const int j1 = min(n_ctx, j0 + chunk);
@@ -289,7 +302,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     // its share). Each warp takes kAttnPos positions of every stage: the score
     // reductions interleave and the running softmax is rescaled once per step.
     extern __shared__ __align__(16) uint8_t attn_smem[];
-    __half* sbuf = reinterpret_cast<__half*>(attn_smem);   // [2][K|V][kAttnStage][head_dim]
+    __half* sbuf = reinterpret_cast<__half*>(attn_smem);   // [2][K (padded rows) | V][kAttnStage]
     constexpr int kPieces = DPL * 32 * 2 / 16;               // 16-byte pieces per row
     const int rows = j1 > j0 ? j1 - j0 : 0;
     const int n_stage = (rows + kAttnStage - 1) / kAttnStage;
@@ -297,12 +310,12 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     const __half* vg = vc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
     auto issue = [&](int st) {
         if (st < n_stage) {
-            __half* sk = sbuf + static_cast<int64_t>(st & 1) * 2 * kAttnStage * head_dim;
-            __half* sv = sk + kAttnStage * head_dim;
+            __half* sk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
+            __half* sv = sk + kAttnStage * KS;
             const int r0 = st * kAttnStage, nr = min(kAttnStage, rows - r0);
             for (int c = threadIdx.x; c < nr * kPieces; c += blockDim.x) {
                 const int r = c / kPieces, o = (c - r * kPieces) * 8;
-                cp_async16(sk + r * head_dim + o, kg + static_cast<int64_t>(r0 + r) * row_stride + o);
+                cp_async16(sk + r * KS + o, kg + static_cast<int64_t>(r0 + r) * row_stride + o);
                 cp_async16(sv + r * head_dim + o, vg + static_cast<int64_t>(r0 + r) * row_stride + o);
             }
         }
@@ -313,46 +326,56 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     for (int st = 0; st < n_stage; ++st) {
         cp_async_wait_one();   // stage st has landed (stage st + 1 may still be in flight)
         __syncthreads();
-        const __half* sk = sbuf + static_cast<int64_t>(st & 1) * 2 * kAttnStage * head_dim;
-        const __half* sv = sk + kAttnStage * head_dim;
+        const __half* sk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
+        const __half* sv = sk + kAttnStage * KS;
         const int jb = j0 + st * kAttnStage + warp * kAttnPos;   // this warp's first position
         if (jb < j1) {
-            HalfVec<DPL> kv[kAttnPos], vv[kAttnPos];
+            const int sb = j0 + st * kAttnStage;   // first position of the stage
+            // scores of the step's 8 positions, four lanes each
+            float a = 0.f;
+            {
+                const int r = min(jb + t8, j1 - 1) - sb;   // past the chunk: repeat, masked
+                const __half* kr = sk + r * KS;
 #pragma unroll
-            for (int t = 0; t < kAttnPos; ++t) {
-                const int j = min(jb + t, j1 - 1) - (j0 + st * kAttnStage);   // past the chunk: repeat, masked
-                kv[t] = load_halves<DPL>(sk + j * head_dim + lane * DPL);
-                vv[t] = load_halves<DPL>(sv + j * head_dim + lane * DPL);
+                for (int c = 0; c < QP; ++c) {
+                    const uint4 kk = *reinterpret_cast<const uint4*>(kr + 8 * (4 * c + qq));
+                    const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
+                    const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
+                    const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&kk.z));
+                    const float2 k3 = __half22float2(*reinterpret_cast<const __half2*>(&kk.w));
+                    a = fmaf(qv[c][0], k0.x, a);
+                    a = fmaf(qv[c][1], k0.y, a);
+                    a = fmaf(qv[c][2], k1.x, a);
+                    a = fmaf(qv[c][3], k1.y, a);
+                    a = fmaf(qv[c][4], k2.x, a);
+                    a = fmaf(qv[c][5], k2.y, a);
+                    a = fmaf(qv[c][6], k3.x, a);
+                    a = fmaf(qv[c][7], k3.y, a);
+                }
+                a += __shfl_xor_sync(0xffffffffu, a, 1);
+                a += __shfl_xor_sync(0xffffffffu, a, 2);
             }
-            float sco[kAttnPos];
-#pragma unroll
-            for (int t = 0; t < kAttnPos; ++t) {
-                float a = 0.f;
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) a = fmaf(qv[i], kv[t].f(i), a);
-                sco[t] = a;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-                for (int t = 0; t < kAttnPos; ++t) sco[t] += __shfl_xor_sync(0xffffffffu, sco[t], o);
-            }
-            float mx = m;
-#pragma unroll
-            for (int t = 0; t < kAttnPos; ++t) {
-                sco[t] = jb + t < j1 ? sco[t] * sc : -INFINITY;
-                mx = fmaxf(mx, sco[t]);
-            }
+            const float sco = jb + t8 < j1 ? a * sc : -INFINITY;
+            float mx = fmaxf(m, sco);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
             const float corr = expf(m - mx);   // 0 on the first step (m = -inf)
-            l *= corr;
+            const float p = expf(sco - mx);    // 0 for a masked position
+            float ps = p;
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+            l = fmaf(l, corr, ps);
 #pragma unroll
             for (int i = 0; i < DPL; ++i) acc[i] *= corr;
 #pragma unroll
             for (int t = 0; t < kAttnPos; ++t) {
-                const float p = expf(sco[t] - mx);   // 0 for a masked row
-                l += p;
+                const float pt = __shfl_sync(0xffffffffu, p, 4 * t);
+                const int r = min(jb + t, j1 - 1) - sb;
+                const HalfVec<DPL> vv = load_halves<DPL>(sv + r * HD + lane * DPL);
 #pragma unroll
-                for (int i = 0; i < DPL; ++i) acc[i] = fmaf(p, vv[t].f(i), acc[i]);
+                for (int i = 0; i < DPL; ++i) acc[i] = fmaf(pt, vv.f(i), acc[i]);
             }
             m = mx;
         }
@@ -551,8 +574,8 @@ cudaError_t attention(const float* q, const void* kc, const void* vc, float* out
     const __half* k = static_cast<const __half*>(kc);
     const __half* v = static_cast<const __half*>(vc);
     const int nh = static_cast<int>(n_head), nkv = static_cast<int>(n_kv_head), c = static_cast<int>(ctx);
-    // two stage buffers of K and V
-    const size_t smem = static_cast<size_t>(2 * kAttnStage) * static_cast<size_t>(head_dim) * 2 * 2;
+    // two stage buffers of K (rows padded by 16 bytes) and V
+    const size_t smem = static_cast<size_t>(2 * kAttnStage) * static_cast<size_t>(2 * head_dim + 8) * 2;
     cudaError_t e = cudaSuccess;
     switch (head_dim) {
         case 64: e = launch_attention<2>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
