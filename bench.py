@@ -434,6 +434,26 @@ def profile_decode(steps: int):
     return 0
 
 
+def profile_batched(steps: int, batch: int):
+    """A few eager batched matvecs (Q4_K 4096 x 11008, `batch` activation rows)
+    on one weight copy, small enough for an ncu capture of one launch."""
+    import torch
+    import hesa_cuda as H
+    dev = torch.device("cuda", 0)
+    n, k = BATCHED_SHAPES[0]
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    w = H.quantize(QT["Q4_K"], torch.randn((n, k), generator=g, device=dev) * 0.02)
+    x = torch.randn((batch, k), generator=g, device=dev)
+    y = torch.empty((batch, n), device=dev)
+    ws = H.make_workspace(QT["Q4_K"], n, k, batch, device=dev)
+    for _ in range(max(steps, 1)):
+        H.qmatvec(QT["Q4_K"], w, x, y=y, workspace=ws)
+    torch.cuda.synchronize()
+    log(f"profile batched done: {steps} launch(es) of B={batch}, outputs finite: {bool(torch.isfinite(y).all())}")
+    return 0
+
+
 # --------------------------------------------------------------------------
 # GPU arm
 # --------------------------------------------------------------------------
@@ -722,6 +742,8 @@ def main():
     ap.add_argument("--impl", default="hesa", choices=["hesa", "reference"])
     ap.add_argument("--profile", action="store_true",
                     help="untimed: build inputs, run --steps plain steps, exit (for ncu captures)")
+    ap.add_argument("--profile-batched", type=int, default=0, metavar="B",
+                    help="run --steps eager batched matvecs with B activation rows (for an ncu capture) and exit")
     ap.add_argument("--profile-decode", action="store_true",
                     help="untimed: a 2-layer model of the 7B decode shapes, --steps eager decode steps "
                          "(for ncu launch lists of one step)")
@@ -735,6 +757,8 @@ def main():
         return run_reference(args, rank, world)
     if args.profile_decode:
         return profile_decode(args.steps)
+    if args.profile_batched:
+        return profile_batched(args.steps, args.profile_batched)
     return run_gpu(args, rank, world, local_rank)
 
 
