@@ -1,5 +1,5 @@
 // xdigits.cuh -- exact integer form of one unit of 256 activations, shared by
-// the batch-1 kernels (qmatvec.cu) and the batched tensor-core kernel (qmm.cu).
+// the batch-1 kernels (qmatvec.cu) and the batched tensor-core kernel (qmm_tc.cu).
 //
 // Per unit, X = rint(x / s) with s = 2^(E-21), E the exponent of the unit's
 // largest |x|, so |X| < 2^22; X is split into three balanced int8 digits,

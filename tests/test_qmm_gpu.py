@@ -1,4 +1,4 @@
-"""Batched matvec on the tensor cores (csrc/qmm.cu) through the C ABI: Q4_K and
+"""Batched matvec on the tensor cores (csrc/qmm_tc.cu, tcgen05) through the C ABI: Q4_K and
 Q5_K weights with 2..33 activation rows against the oracle (rel-L2 <= 1e-5
 per activation row), at the batched-decode shapes (4096 x 11008 and
 11008 x 4096, B in {2, 4, 8, 16}), ragged tiles, one-unit and 128-unit rows,
