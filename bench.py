@@ -20,8 +20,11 @@ Metric: algorithmic bytes (packed W + x + y) per second, whole job.
 
 N > 1 GPUs (torchrun): weak scaling with row-sharded weights -- rank r holds
 rows [r*n, (r+1)*n) of an N-times taller matrix (its shard has the N=1 shape)
-and every step ends with one NCCL all-gather of all eight y slices, so every
-rank holds the full outputs.
+and every rank ends each step holding the full outputs: the matvec kernels
+store their rows straight into every rank's gathered buffer over NVLink
+(hesa_cuda_qmatvec_gather) and one barrier kernel per step publishes
+completion (hesa_cuda_peer_barrier). The same step with an NCCL all-gather
+instead is timed beside it ("nccl_allgather").
 
 --impl reference: times the reference CPU path (above) on rank 0 only.
 """
@@ -489,6 +492,21 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     # the full (all-gathered) outputs of one step
     y_local = torch.empty(sum(n for _, _, n, _, _, _, _, _ in dmats), dtype=torch.float32, device=dev)
     y_all = torch.empty(world * y_local.numel(), dtype=torch.float32, device=dev)
+    peers, targets = None, []
+    if world > 1:
+        # gathered buffers shared over NVLink, laid out as NCCL's all-gather of
+        # y_local lays them out: rank r's block of all eight outputs at r * rows
+        import sharding
+        peers = sharding.PeerGather(y_all.numel(), rank, world, device=dev)
+        off = rank * y_local.numel()
+        for name, qt, n, k, wt, xt, yt, ws in dmats:
+            targets.append(peers.targets(off))
+            off += n
+        pg.barrier()
+
+    def barrier_count():
+        torch.cuda.synchronize(dev)
+        return int(H.device_view(peers.epoch, 1, device=dev, dtype="<i4")[0])
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -496,13 +514,20 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             H.qmatvec(qt, wt, xt, y=yt, workspace=ws)
         stream.synchronize()
 
-    def one_step():
+    def one_step_nccl():
         off = 0
         for name, qt, n, k, wt, xt, yt, ws in dmats:
             H.qmatvec(qt, wt, xt, y=y_local[off:off + n], workspace=ws, stream=stream)
             off += n
         if pg is not None:
             pg.all_gather_into_tensor(y_all, y_local)
+
+    def one_step():
+        if peers is None:
+            return one_step_nccl()
+        for (name, qt, n, k, wt, xt, yt, ws), tgt in zip(dmats, targets):
+            H.qmatvec_gather(qt, wt, xt, tgt, world, peers.epoch, stream=stream)
+        H.peer_barrier(peers.flags, rank, world, peers.epoch, stream=stream)
 
     if args.profile:
         # a short, untimed run for ncu: K plain steps (8 launches each), no graphs
@@ -533,11 +558,18 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         sampler = ClockSampler(local_rank) if rank == 0 else None
         if sampler:
             sampler.start()
-        t_end = time.time() + 2.0
-        while time.time() < t_end:
-            for _ in range(200):
-                graph.replay()
-            stream.synchronize()
+        # the same number of replays on every rank (each step ends in a
+        # cross-rank barrier), sized to ~2 s from a short timed run
+        t0 = time.time()
+        for _ in range(50):
+            graph.replay()
+        stream.synchronize()
+        n_load = torch.tensor([int(2.0 / max((time.time() - t0) / 50, 1e-6))], device=dev)
+        if pg is not None:
+            pg.all_reduce(n_load, op=pg.ReduceOp.MAX)
+        for _ in range(min(int(n_load.item()), 100000)):
+            graph.replay()
+        stream.synchronize()
 
         if pg is not None:
             pg.barrier()
@@ -552,6 +584,27 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
         dt_ms = ev0.elapsed_time(ev1)
         clocks = sampler.stop() if sampler else None
+
+        # the same step with NCCL's all-gather instead of the fused one
+        nccl_ms = None
+        if pg is not None:
+            gn = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gn, stream=stream):
+                one_step_nccl()
+            for _ in range(3):
+                gn.replay()
+            stream.synchronize()
+            pg.barrier()
+            torch.cuda.synchronize(dev)
+            en0 = torch.cuda.Event(enable_timing=True)
+            en1 = torch.cuda.Event(enable_timing=True)
+            en0.record(stream)
+            for _ in range(args.steps):
+                gn.replay()
+            en1.record(stream)
+            en1.synchronize()
+            nccl_ms = en0.elapsed_time(en1)
+            del gn
 
         # kernel-only time of the same step without the collective (roofline)
         if pg is not None:
@@ -614,18 +667,24 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         h2d = x_host.numel() * 4
         d2h = y_host.numel() * 4
 
-        def e2e_body():
+        def e2e_body(parity=0):
+            # parity: which of the two gathered buffers this step fills (N > 1)
             x_all.copy_(x_host, non_blocking=True)
-            off = 0
-            for name, qt, n, k, wt, xt, yt, ws in dmats:
-                H.qmatvec(qt, wt, xt, y=y_local[off:off + n], workspace=ws, stream=stream)
-                off += n
-            if pg is not None:
-                pg.all_gather_into_tensor(y_all, y_local)
-            y_host.copy_(y_out, non_blocking=True)
+            if peers is None:
+                off = 0
+                for name, qt, n, k, wt, xt, yt, ws in dmats:
+                    H.qmatvec(qt, wt, xt, y=y_local[off:off + n], workspace=ws, stream=stream)
+                    off += n
+                y_host.copy_(y_out, non_blocking=True)
+            else:
+                one_step()
+                y_host.copy_(peers.output(parity), non_blocking=True)
+
+        count = [barrier_count() if peers is not None else 0]
 
         def e2e_step():
-            e2e_body()
+            e2e_body(count[0] & 1)
+            count[0] += 1
             stream.synchronize()
 
         # eager: every call from Python, as a notebook user would make them
@@ -644,32 +703,45 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
         # graphed: the same public-API calls and copies captured once, as a
         # serving loop runs its decode step; each replay copies x in from
-        # pinned host memory and y back out, and the host waits for it
+        # pinned host memory and y back out, and the host waits for it. At
+        # N > 1 a replay holds two steps, one per gathered buffer, so the
+        # buffer each copy reads stays the one its step filled.
+        per_replay = 1 if peers is None else 2
         g_e2e = torch.cuda.CUDAGraph()
+        p0 = count[0] & 1
         with torch.cuda.graph(g_e2e, stream=stream):
-            e2e_body()
+            for j in range(per_replay):
+                e2e_body((p0 + j) & 1)
         for _ in range(3):
             g_e2e.replay()
             stream.synchronize()
         if pg is not None:
             pg.barrier()
+        replays = max(1, args.steps // per_replay)
         ee0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(replays):
             g_e2e.replay()
             stream.synchronize()
         ee1.record(stream)
         ee1.synchronize()
-        e2e_ms = ee0.elapsed_time(ee1)
+        e2e_ms = ee0.elapsed_time(ee1) * args.steps / (replays * per_replay)
+        if peers is not None:
+            # the gathered outputs equal the NCCL-gathered ones
+            one_step_nccl()
+            stream.synchronize()
+            par = (barrier_count() - 1) & 1
+            gathered_ok = bool(torch.equal(peers.output(par), y_all))
 
     # the 7B-shaped Q4_K decode step, one full replica per rank
     dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg)
     batched = run_batched(dev, stream) if rank == 0 else None
 
     # max over ranks
-    times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec["ms"]], dtype=torch.float64, device=dev)
+    times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec["ms"], nccl_ms or 0.0,
+                          0.0 if peers is None or gathered_ok else 1.0], dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
-    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms = (float(v) for v in times.cpu())
+    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms, nccl_ms, gather_bad = (float(v) for v in times.cpu())
 
     if rank == 0:
         bytes_step = step_bytes() * world
@@ -691,7 +763,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             "config": {"workload": "per-type matvec sweep Q8_0/Q4_K/Q5_K/Q6_K x {4096x11008, 11008x4096} "
                                    "([n_out x k]), batch 1",
                        "bytes_per_step_per_gpu": step_bytes(), "l2": L2_NOTE,
-                       "parallelism": (f"row-sharded weights x{world}, NCCL all-gather of y" if world > 1
+                       "parallelism": (f"row-sharded weights x{world}, all-gather of y fused into the matvec "
+                                       "(peer stores over NVLink + one barrier kernel per step)" if world > 1
                                        else "single GPU"),
                        "timing": "CUDA graph of one step, replayed K times between CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -699,14 +772,20 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                          "traffic": traffic,
                          "kernel": "qmv_strip_kernel (8 launches per step)"},
             "per_type_gbs": per_type,
+            "nccl_allgather": ({"value": round(bytes_step * args.steps / (nccl_ms * 1e-3) / 1e9, 1),
+                                "ms_per_step": round(nccl_ms / args.steps, 4),
+                                "how": "the same step with local outputs and NCCL all_gather_into_tensor",
+                                "gathered_outputs_equal": gather_bad == 0.0}
+                               if world > 1 else None),
             "pct_of_8tbs": round(achieved / 8000.0, 4),
             "e2e": {"value": round(bytes_step * args.steps / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-                    "how": "hesa_cuda.qmatvec per matrix; every step one copy of all activations from "
-                           "pinned host memory and one copy of all outputs back, captured once in a CUDA "
-                           "graph and replayed with a host synchronize per step",
+                    "how": "hesa_cuda.qmatvec per matrix (hesa_cuda.qmatvec_gather + peer_barrier at N > 1); "
+                           "every step one copy of all activations from pinned host memory and one copy of "
+                           "all outputs back, captured once in a CUDA graph and replayed with a host "
+                           "synchronize per replay",
                     "eager_value": round(bytes_step * args.steps / (e2e_eager_ms * 1e-3) / 1e9, 1)},
-            "gpu_launches": len(SWEEP) * args.steps,
+            "gpu_launches": (len(SWEEP) + (1 if world > 1 else 0)) * args.steps,
             "decode": {"model": "Llama-shaped 7B (32 layers, d_model 4096, 32 heads x 128, FFN 11008 SwiGLU, "
                                 "vocab 32000, RMSNorm, RoPE 10000), Q4_K, random init N(0, 0.02)",
                        "ctx": DECODE_7B["ctx"], "pos": DECODE_POS,
@@ -729,6 +808,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     del graph, g_e2e   # graphs that hold NCCL calls go before the process group
     if pg is not None:
+        torch.cuda.synchronize(dev)
+        pg.barrier()
+        if peers is not None:
+            peers.close()
         pg.barrier()
         pg.destroy_process_group()
     return 0

@@ -12,6 +12,7 @@
 #include "qtypes.cuh"
 
 #include <algorithm>
+#include <cstring>
 #include <string>
 
 namespace {
@@ -120,6 +121,79 @@ int hesa_cuda_quantize(int qtype, const float* src, int64_t n_rows, int64_t k, i
     cudaError_t e = hesa_cuda::quantize(qtype, src, n_rows, k, ld_src, dst, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "quantize kernel");
     return HESA_CUDA_OK;
+}
+
+int hesa_cuda_peer_alloc(size_t bytes, void** dev_ptr_out, void* handle_out) {
+    if (!dev_ptr_out || !handle_out || bytes == 0) return fail(HESA_CUDA_INVALID_ARGUMENT, "bad peer_alloc arguments");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "peer_alloc cudaMalloc");
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "peer_alloc");
+    }
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    std::memcpy(handle_out, &h, sizeof(h));
+    *dev_ptr_out = p;
+    return HESA_CUDA_OK;
+}
+
+int hesa_cuda_peer_free(void* dev_ptr) {
+    if (!dev_ptr) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    const cudaError_t e = cudaFree(dev_ptr);
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "peer_free");
+}
+
+int hesa_cuda_peer_open(const void* handle, void** dev_ptr_out) {
+    if (!handle || !dev_ptr_out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "peer_open");
+}
+
+int hesa_cuda_peer_close(void* dev_ptr) {
+    if (!dev_ptr) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "peer_close");
+}
+
+int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
+                             float* const* y_peers, int world, const uint32_t* epoch, void* stream) {
+    if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
+    if (!w || !x || !y_peers || !epoch) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (world < 1 || world > hesa_cuda::kMaxPeers) return fail(HESA_CUDA_INVALID_ARGUMENT, "world must be 1..8");
+    if (n_rows <= 0 || k <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "non-positive dimension");
+    if (n_rows >= (int64_t(1) << 30) || k % 256 != 0)
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "gathered matvec needs k a multiple of 256");
+    if (!aligned16(w) || !aligned16(x)) return fail(HESA_CUDA_INVALID_ARGUMENT, "W and x must be 16-byte aligned");
+    if (!hesa_cuda::qmv_strip_eligible(qtype, w, n_rows, k))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "gathered matvec needs k <= 24576");
+    hesa_cuda::PeerOut out = {};
+    for (int b = 0; b < 2; ++b)
+        for (int p = 0; p < world; ++p) {
+            if (!y_peers[b * world + p]) return fail(HESA_CUDA_INVALID_ARGUMENT, "null output pointer");
+            out.y[b][p] = y_peers[b * world + p];
+        }
+    out.epoch = epoch;
+    out.world = world;
+    const cudaError_t e =
+        hesa_cuda::qmv_strip_gather(qtype, w, n_rows, k, x, scale, out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "gathered matvec kernel");
+}
+
+int hesa_cuda_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch, void* stream) {
+    if (!flags || !epoch) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (world < 1 || world > hesa_cuda::kMaxPeers || rank < 0 || rank >= world)
+        return fail(HESA_CUDA_INVALID_ARGUMENT, "bad rank / world");
+    for (int p = 0; p < world; ++p)
+        if (!flags[p]) return fail(HESA_CUDA_INVALID_ARGUMENT, "null flag pointer");
+    const cudaError_t e = hesa_cuda::peer_barrier(flags, rank, world, epoch, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "peer barrier kernel");
 }
 
 int hesa_cuda_device_status(void* stream, int* status_out) {

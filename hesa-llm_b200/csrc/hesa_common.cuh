@@ -18,6 +18,7 @@ enum : int {
     kStatusWaitTimeout = 1,     // a stage's bulk copy did not land in time
     kStatusDrainTimeout = 2,    // a copy still in flight during the error exit
     kStatusBadPosition = 3,     // a device-side position outside the cache / rope table
+    kStatusPeerTimeout = 4,     // a peer rank did not reach the all-gather barrier in time
 };
 
 constexpr unsigned long long HESA_WAIT_LIMIT_NS = 2000000000ull;  // 2 s

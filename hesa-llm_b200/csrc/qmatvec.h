@@ -41,6 +41,28 @@ cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, 
                             const float* norm_w, float eps, float* y, const float* resid, float scale,
                             cudaStream_t stream);
 
+// Row-sharded matvec with the all-gather fused into the epilogue: a rank's
+// strip kernel stores its rows straight into the gathered output buffer of
+// every rank (its own and its peers', mapped over NVLink with CUDA IPC).
+// Buffers alternate by the parity of the rank's barrier count (peer_barrier
+// increments it), so a rank may write step s + 1 into a peer while that peer
+// still reads step s.
+constexpr int kMaxPeers = 8;
+struct PeerOut {
+    float* y[2][kMaxPeers];   // [parity][rank]: where this shard's row 0 lands in that rank's buffer
+    const uint32_t* epoch;    // this rank's barrier count (device); parity = *epoch & 1
+    int world;                // number of ranks; 0 = plain output
+};
+cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
+                             const PeerOut& out, cudaStream_t stream);
+
+// Completion of the fused all-gathers of one step: every rank publishes
+// *epoch + 1 into slot `rank` of every rank's flags (release, system scope),
+// waits until all `world` slots of its own flags reach that value (acquire,
+// bounded: on timeout the status word records kStatusPeerTimeout), then
+// stores it into *epoch. flags[p] is rank p's flag array as mapped here.
+cudaError_t peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch, cudaStream_t stream);
+
 // One warp per row, any k that is a multiple of the block size.
 cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,
                         int64_t batch, float* y, int64_t ldy, float scale, cudaStream_t stream);

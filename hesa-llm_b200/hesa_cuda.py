@@ -69,6 +69,12 @@ SIGNATURES = [
     ("hesa_cuda_embed", _int, [_int, _vp, _i64, _i64, _vp, _vp, _vp]),
     ("hesa_cuda_decode_step", _int, [ctypes.POINTER(Model), ctypes.POINTER(Layer), _vp, _vp, _vp, ctypes.c_int32,
                                      _vp, _vp, _vp, _vp, _sz, _vp]),
+    ("hesa_cuda_peer_alloc", _int, [_sz, ctypes.POINTER(_vp), _vp]),
+    ("hesa_cuda_peer_free", _int, [_vp]),
+    ("hesa_cuda_peer_open", _int, [_vp, ctypes.POINTER(_vp)]),
+    ("hesa_cuda_peer_close", _int, [_vp]),
+    ("hesa_cuda_qmatvec_gather", _int, [_int, _vp, _i64, _i64, _vp, _f, ctypes.POINTER(_vp), _int, _vp, _vp]),
+    ("hesa_cuda_peer_barrier", _int, [ctypes.POINTER(_vp), _int, _int, _vp, _vp]),
 ]
 
 
@@ -175,6 +181,60 @@ def quantize(qtype: int, x, out=None, stream=None):
     _check(lib().hesa_cuda_quantize(qtype, x2.data_ptr(), n_rows, k, x2.stride(0), out.data_ptr(),
                                     _stream_handle(stream)))
     return out
+
+
+# ---- row-sharded matvec with the all-gather fused in (hesa_cuda_qmatvec_gather) ----
+
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """A zero-filled device allocation shared with the other ranks of the node:
+    (device pointer, 64-byte CUDA IPC handle)."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    _check(lib().hesa_cuda_peer_alloc(nbytes, ctypes.byref(ptr), handle))
+    return ptr.value, handle.raw
+
+
+def peer_free(ptr: int) -> None:
+    _check(lib().hesa_cuda_peer_free(ptr))
+
+
+def peer_open(handle: bytes) -> int:
+    """Map another rank's peer_alloc allocation into this process."""
+    ptr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(handle), 64)
+    _check(lib().hesa_cuda_peer_open(buf, ctypes.byref(ptr)))
+    return ptr.value
+
+
+def peer_close(ptr: int) -> None:
+    _check(lib().hesa_cuda_peer_close(ptr))
+
+
+def qmatvec_gather(qtype: int, w, x, y_peers, world: int, epoch: int, scale: float = 1.0, stream=None):
+    """This rank's rows of y = scale * W x (w: its packed rows [n_rows, row_bytes],
+    x [k]) stored into every rank's gathered buffer: y_peers lists 2 * world
+    device addresses (parity-major) of this shard's first row in each rank's
+    buffer; epoch is the device address of this rank's barrier count."""
+    n_rows, k = w.shape[0], x.shape[-1]
+    arr = (ctypes.c_void_p * (2 * world))(*y_peers)
+    _check(lib().hesa_cuda_qmatvec_gather(qtype, w.data_ptr(), n_rows, k, x.data_ptr(), float(scale), arr, world,
+                                          epoch, _stream_handle(stream)))
+
+
+def peer_barrier(flags, rank: int, world: int, epoch: int, stream=None) -> None:
+    arr = (ctypes.c_void_p * world)(*flags)
+    _check(lib().hesa_cuda_peer_barrier(arr, rank, world, epoch, _stream_handle(stream)))
+
+
+def device_view(ptr: int, numel: int, device=None, dtype: str = "<f4"):
+    """A torch tensor over raw device memory (no copy), through the CUDA array
+    interface."""
+    import torch
+
+    class _View:
+        __cuda_array_interface__ = {"shape": (numel,), "typestr": dtype, "data": (ptr, False), "version": 3,
+                                    "strides": None}
+    return torch.as_tensor(_View(), device=device or "cuda")
 
 
 def device_status(stream=None) -> int:

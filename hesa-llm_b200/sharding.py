@@ -3,10 +3,17 @@
 Output rows of y = W x are independent: rank r holds the contiguous rows
 [r0, r1) of W (packed GGUF rows, balanced to one row, the same split the strip
 kernel uses between its CTAs), computes y[r0:r1], and the full y is
-all-gathered so every rank holds it. NCCL's all_gather_into_tensor wants equal
-sizes, so every rank contributes a slot of ceil(n_out / world) rows and the
-gathered buffer is compacted back to n_out rows with one index_select (a no-op
-view when world divides n_out).
+all-gathered so every rank holds it. Two ways to gather:
+
+* "peer" (default on GPUs): the matvec kernel itself stores its rows into the
+  gathered buffer of every rank over NVLink (CUDA IPC mappings,
+  hesa_cuda_qmatvec_gather) and one barrier kernel per step publishes
+  completion (hesa_cuda_peer_barrier). No padding: each rank writes at its own
+  row offset.
+* "nccl": NCCL's all_gather_into_tensor, which wants equal sizes, so every
+  rank contributes a slot of ceil(n_out / world) rows and the gathered buffer
+  is compacted back to n_out rows with one index_select (a no-op view when
+  world divides n_out). Also what the CPU (gloo) tests run.
 """
 from __future__ import annotations
 
@@ -69,3 +76,92 @@ class ShardedQMatvec:
             self.y_slot.mul_(scale)
         dist.all_gather_into_tensor(self.y_all, self.y_slot, group=self.group)
         return self.y_all if self.index is None else self.y_all.index_select(0, self.index)
+
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
+
+
+class PeerGather:
+    """Gathered output buffers shared by the ranks of one node.
+
+    Each rank allocates (hesa_cuda_peer_alloc) two parities of an `out_rows`
+    fp32 buffer, a flag array of `world` slots and its barrier count, and maps
+    every other rank's allocation from the CUDA IPC handles exchanged through
+    `group`. Matvecs of a step store into parity `step & 1` of every rank
+    (PeerGather.targets gives their addresses); barrier() ends the step.
+    """
+
+    def __init__(self, out_rows: int, rank: int, world: int, group=None, device=None):
+        import torch.distributed as dist
+        import hesa_cuda as H
+        if not 1 <= world <= 8 or not 0 <= rank < world:
+            raise ValueError(f"bad rank {rank} / world {world}")
+        self.out_rows, self.rank, self.world = out_rows, rank, world
+        self.y_bytes = _align(4 * out_rows)
+        self.flag_off = 2 * self.y_bytes
+        self.epoch_off = self.flag_off + _align(4 * world)
+        self.local, handle = H.peer_alloc(self.epoch_off + 256)
+        handles = [handle]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle, group=group)
+        self.base = [self.local if p == rank else H.peer_open(handles[p]) for p in range(world)]
+        self.flags = [b + self.flag_off for b in self.base]
+        self.epoch = self.local + self.epoch_off
+        self.steps = 0      # barriers issued from the host (graph replays are counted by the caller)
+        self.device = device
+
+    def targets(self, row0: int) -> list[int]:
+        """Addresses (parity-major, then rank) where row `row0` of the
+        gathered output lives in every rank's buffers."""
+        return [b + par * self.y_bytes + 4 * row0 for par in (0, 1) for b in self.base]
+
+    def barrier(self, stream=None) -> None:
+        import hesa_cuda as H
+        H.peer_barrier(self.flags, self.rank, self.world, self.epoch, stream=stream)
+        self.steps += 1
+
+    def output(self, parity: int):
+        """This rank's gathered buffer of the given parity (a torch view)."""
+        import hesa_cuda as H
+        return H.device_view(self.local + parity * self.y_bytes, self.out_rows, device=self.device)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then free this rank's (call on every rank,
+        after a collective barrier, once no kernel uses them)."""
+        import hesa_cuda as H
+        for p, b in enumerate(self.base):
+            if p != self.rank:
+                H.peer_close(b)
+        H.peer_free(self.local)
+        self.base = []
+
+
+class GatheredQMatvec:
+    """y = scale * W x with W's rows split over the ranks, the all-gather fused
+    into the matvec (PeerGather). Every rank calls it with the same x and gets
+    the full y (a view valid until the call after next)."""
+
+    def __init__(self, qtype: int, w_rows, n_out: int, k: int, rank: int, world: int, group=None, peers=None,
+                 row_offset: int = 0):
+        self.qtype, self.n_out, self.k, self.rank, self.world = qtype, n_out, k, rank, world
+        self.r0, self.r1 = row_range(n_out, rank, world)
+        if w_rows.shape[0] != self.r1 - self.r0:
+            raise ValueError(f"rank {rank} holds {w_rows.shape[0]} rows, its shard has {self.r1 - self.r0}")
+        self.w = w_rows
+        self.own = peers is None
+        self.peers = peers or PeerGather(n_out, rank, world, group=group, device=w_rows.device)
+        self.row_offset = row_offset
+        self.tgt = self.peers.targets(row_offset + self.r0)
+
+    def launch(self, x, scale: float = 1.0, stream=None) -> None:
+        """Only the matvec (several may share one barrier)."""
+        import hesa_cuda as H
+        H.qmatvec_gather(self.qtype, self.w, x, self.tgt, self.world, self.peers.epoch, scale=scale, stream=stream)
+
+    def __call__(self, x, scale: float = 1.0, stream=None):
+        par = self.peers.steps & 1
+        self.launch(x, scale, stream)
+        self.peers.barrier(stream)
+        return self.peers.output(par)[self.row_offset:self.row_offset + self.n_out]

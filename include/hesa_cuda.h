@@ -264,9 +264,53 @@ HESA_CUDA_API int hesa_cuda_decode_step(const hesa_cuda_model* model, const hesa
 /* Sticky device-side status of the kernels: 0 while nothing has gone wrong
  * in this process, else the first code recorded: 1 a bulk copy did not land
  * within the bounded wait, 2 a copy was still in flight when the kernel
- * gave up, 3 a device-side position outside the KV cache or the rope table.
+ * gave up, 3 a device-side position outside the KV cache or the rope table,
+ * 4 a peer rank did not reach hesa_cuda_peer_barrier in time.
  * Reading synchronizes `stream`. hesa_cuda_clear_device_status resets it. */
 HESA_CUDA_API int hesa_cuda_device_status(void* stream, int* status_out);
+
+/* ---- row-sharded matvec with the output all-gather fused in ----
+ * The rows of W are split over the GPUs of one node (rank r holds rows
+ * [r0, r1)); every rank needs all of y. Replaces the NCCL all-gather that
+ * follows a sharded CPU_Backend::matmul-equivalent call
+ * (src/backend/cpu_backend.cpp:24-41 computes the unsharded product): each
+ * rank's kernel stores its rows straight into the gathered buffer of every
+ * rank over NVLink, and one barrier per step publishes completion. No
+ * counterpart in the reference, which runs on one device.
+ *
+ * hesa_cuda_peer_alloc: the one entry point that allocates. cudaMalloc of
+ * `bytes` (zero-filled) on the current device; *handle_out (host, 64 bytes)
+ * receives its CUDA IPC handle for the other ranks. Free with
+ * hesa_cuda_peer_free after every peer has closed it.
+ * hesa_cuda_peer_open / hesa_cuda_peer_close: map / unmap another rank's
+ * allocation from its 64-byte handle (not one from this process). */
+HESA_CUDA_API int hesa_cuda_peer_alloc(size_t bytes, void** dev_ptr_out, void* handle_out);
+HESA_CUDA_API int hesa_cuda_peer_free(void* dev_ptr);
+HESA_CUDA_API int hesa_cuda_peer_open(const void* handle, void** dev_ptr_out);
+HESA_CUDA_API int hesa_cuda_peer_close(void* dev_ptr);
+
+/* y_shard = scale * W_shard . x for this rank's n_rows rows of W (batch 1;
+ * k a multiple of 256, k <= 24576; W, x 16-byte aligned), stored into all
+ * `world` ranks at once: row i goes to y_peers[b * world + p][i] for every p,
+ * where y_peers (host array of 2 * world device pointers, as mapped in this
+ * process) points at this shard's first row inside rank p's gathered buffer
+ * for parity b, and b = *epoch & 1 (epoch: this rank's barrier count, device,
+ * written by hesa_cuda_peer_barrier). Two parities let a rank store step s + 1
+ * while a peer still reads step s; a gathered result stays valid until the
+ * barrier of the step after next. */
+HESA_CUDA_API int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x,
+                                           float scale, float* const* y_peers, int world, const uint32_t* epoch,
+                                           void* stream);
+
+/* End of a step of gathered matvecs: publishes *epoch + 1 into slot `rank`
+ * of every rank's flag array (flags: host array of `world` device pointers to
+ * uint32[world], flags[p] = rank p's array as mapped here, flags[rank] this
+ * rank's own), waits until every slot of this rank's array holds it, then
+ * stores it into *epoch. Every rank must issue the same sequence of steps;
+ * the wait is bounded (2 s, device status 4 on expiry), so the ranks must
+ * reach it within that time of one another. */
+HESA_CUDA_API int hesa_cuda_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch,
+                                         void* stream);
 HESA_CUDA_API int hesa_cuda_clear_device_status(void* stream);
 
 /* Last error message recorded on this host thread ("" if none). */

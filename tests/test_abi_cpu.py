@@ -107,3 +107,43 @@ def test_error_type_carries_reference_code():
     with pytest.raises(H.HesaError) as ei:
         H._check(6)
     assert ei.value.code == 6 and "SHAPE_MISMATCH" in str(ei.value)
+
+
+def gather_call(qt=12, w=FAKE, n=64, k=256, x=FAKE, peers=(FAKE,) * 4, world=2, epoch=FAKE):
+    arr = (ctypes.c_void_p * len(peers))(*peers) if peers is not None else None
+    return H.lib().hesa_cuda_qmatvec_gather(qt, w, n, k, x, 1.0, arr, world, epoch, None)
+
+
+@pytest.mark.parametrize("kwargs,code", [
+    (dict(qt=3), 3),
+    (dict(w=0), 2),
+    (dict(x=0), 2),
+    (dict(epoch=0), 2),
+    (dict(peers=None), 2),
+    (dict(world=0), 2),
+    (dict(world=9, peers=(FAKE,) * 18), 2),
+    (dict(n=0), 6),
+    (dict(k=96, qt=2), 6),           # gathered path needs whole 256-weight units
+    (dict(w=FAKE + 8), 2),
+    (dict(x=FAKE + 4), 2),
+])
+def test_gathered_matvec_rejects_bad_arguments_without_launching(kwargs, code):
+    assert gather_call(**kwargs) == code
+    assert H.lib().hesa_cuda_last_error()
+
+
+def test_peer_barrier_and_alloc_reject_bad_arguments():
+    L = H.lib()
+    two = (ctypes.c_void_p * 2)(FAKE, FAKE)
+    assert L.hesa_cuda_peer_barrier(two, 2, 2, FAKE, None) == 2      # rank outside world
+    assert L.hesa_cuda_peer_barrier(two, 0, 0, FAKE, None) == 2
+    assert L.hesa_cuda_peer_barrier(two, 0, 9, FAKE, None) == 2
+    assert L.hesa_cuda_peer_barrier(two, 0, 2, None, None) == 2
+    assert L.hesa_cuda_peer_barrier((ctypes.c_void_p * 2)(FAKE, 0), 0, 2, FAKE, None) == 2
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    assert L.hesa_cuda_peer_alloc(0, ctypes.byref(ptr), handle) == 2
+    assert L.hesa_cuda_peer_alloc(256, None, handle) == 2
+    assert L.hesa_cuda_peer_open(None, ctypes.byref(ptr)) == 2
+    assert L.hesa_cuda_peer_close(None) == 2
+    assert L.hesa_cuda_peer_free(None) == 2
