@@ -608,7 +608,7 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
 //   * Lane (slice s, quarter-column q) owns 64 weights of every row r with
 //     r = s (mod slices): unit q/4, quarter q%4. It loads that quarter of x
 //     once and keeps it in registers for all its rows. Whole warps belong to
-//     one slice.
+//     one slice; its quarter-columns are spread evenly over them.
 //   * Per row, a warp's lanes are reduced with shuffles and lane 0 stores
 //     the warp's partial in shared memory; at the end the CTA adds the warps'
 //     partials of each row in a fixed order. No workspace, deterministic.
@@ -617,6 +617,12 @@ qmv_stream_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* 
 // ---------------------------------------------------------------------------
 
 constexpr int kStripMaxSlots = 16;
+
+// Rows decoded together per group: four independent chains, three for the
+// types whose quarter needs the most registers (Q5_K, Q6_K: four rows at once
+// would exceed the 168 registers a thread has at 384 threads; measured 2,818
+// vs 2,694 GB/s on Q6_K).
+__host__ __device__ constexpr int strip_group_rows(int qt) { return (qt == kQ6_K || qt == kQ5_K) ? 3 : 4; }
 constexpr int kStripBatch = 4;   // units of x one warp loads at a time
 constexpr int kStripSmemMax = 226 * 1024;
 
@@ -688,9 +694,13 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     const int active_warps = RS * wps;
     const int slice = warp / wps;
     const int wq = warp - slice * wps;         // warp index inside its slice
-    const int q = wq * 32 + lane;
+    // quarter-columns spread evenly over the slice's warps (e.g. 172 as 5 x 29
+    // + 27, not 5 x 32 + 12), so no scheduler partition gets more than its
+    // share of the decode
+    const int lpw = (QC + wps - 1) / wps;
+    const int q = wq * lpw + lane;
     const bool wactive = slice < RS;
-    const bool qactive = wactive && q < QC;
+    const bool qactive = wactive && lane < lpw && q < QC;
     const int unit = q >> 2, qc = q & 3;
     const int r0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_out / gridDim.x);
     const int r1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_out / gridDim.x);
@@ -839,24 +849,26 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
             const int lr1 = min(nrows, lr0 + CR);
             const uint8_t* base = slots + static_cast<size_t>(slot) * slot_stride +
                                   ((static_cast<size_t>(r0 + lr0) * pitch) & 15) + static_cast<size_t>(unit) * UB;
-            // this slice's rows of the chunk, four at a time: independent
-            // decode chains, then one transposing reduction for the four.
+            // this slice's rows of the chunk, GR at a time: independent
+            // decode chains, then one transposing reduction for the group.
             // The row count of a group is warp-uniform; each count has its
             // own code so no decode is issued for a missing row.
-            for (int i0 = lr0 + slice; i0 < lr1; i0 += 4 * RS) {
+            constexpr int GR = strip_group_rows(QT);
+            for (int i0 = lr0 + slice; i0 < lr1; i0 += GR * RS) {
                 float a[4] = {0.f, 0.f, 0.f, 0.f};
                 const uint8_t* rb = base + static_cast<size_t>(i0 - lr0) * pitch;
                 const size_t rstep = static_cast<size_t>(RS) * pitch;
                 const int nv = (lr1 - i0 + RS - 1) / RS;
                 if (qactive) {
-                    if (nv >= 4) strip_rows<QT, 4>(rb, rstep, qc, xq, a);
+                    if (nv >= GR) strip_rows<QT, GR>(rb, rstep, qc, xq, a);
                     else if (nv == 3) strip_rows<QT, 3>(rb, rstep, qc, xq, a);
                     else if (nv == 2) strip_rows<QT, 2>(rb, rstep, qc, xq, a);
                     else strip_rows<QT, 1>(rb, rstep, qc, xq, a);
                 }
-                const int row = i0 + RS * reduce4_row(lane);
+                const int rr = reduce4_row(lane);
+                const int row = i0 + RS * rr;
                 const float tot = reduce4(a, lane);
-                if ((lane & 7) == 0 && row < lr1) part[row * wps + wq] = tot;
+                if ((lane & 7) == 0 && rr < GR && row < lr1) part[row * wps + wq] = tot;
             }
             __syncwarp();
             if (lane == 0) {
