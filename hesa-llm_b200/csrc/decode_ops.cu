@@ -267,17 +267,40 @@ __device__ __forceinline__ HalfVec<DPL> load_halves(const __half* p) {
 // in registers; two shuffles combine the four partial dots. The step's
 // maximum and sum run over the lanes 4 apart (three shuffles each), one
 // exponential per lane. P . V: lane owns head_dim/32 consecutive dims.
-template <int DPL>  // dims per lane (head_dim / 32)
+// With ROPE, the kernel also does the work of rope_kv_kernel for the decode
+// step: q arrives unrotated and is rotated in registers (the pair (d, d +
+// head_dim/2) sits in one lane), and the CTA whose chunk holds slot
+// pos % ctx rotates this token's k, rounds k and v to fp16, puts them into
+// that row of its shared-memory stage (over whatever the copy brought) and,
+// for the first query head of each KV head, into the cache. Rounding as
+// rope_kv_kernel, so the result equals rope_kv followed by the plain kernel.
+struct AttnRope {
+    const float* k_new;   // this token's k [n_kv_head * head_dim] (unrotated)
+    const float* v_new;   // this token's v [n_kv_head * head_dim]
+    __half* kc;           // the caches, written at slot pos % ctx
+    __half* vc;
+    const float* table;   // rope table [table_rows][head_dim]: cos, then sin
+    int table_rows;
+    int* status;
+};
+
+template <int DPL, bool ROPE>  // dims per lane (head_dim / 32)
 __global__ void __launch_bounds__(kAttnWarps * 32)
 attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
                  float* __restrict__ out, int n_head, int n_kv_head, int ctx, const int32_t* __restrict__ pos_dev,
-                 int32_t pos_host, int chunk, float* __restrict__ part, int* __restrict__ counters) {
+                 int32_t pos_host, int chunk, float* __restrict__ part, int* __restrict__ counters, AttnRope ri) {
     const int head_dim = DPL * 32;
     constexpr int HD = DPL * 32, KS = HD + 8;   // K rows in halves, padded by 16 bytes
     constexpr int QP = HD / 8 / 4;              // 16-byte pieces of q per lane
     const int h = blockIdx.x, split = blockIdx.y, n_split = gridDim.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int32_t pos = pos_dev ? *pos_dev : pos_host;
+    if constexpr (ROPE) {
+        if (pos < 0 || pos >= ri.table_rows) {   // uniform: every CTA leaves, no counter is touched
+            if (h == 0 && split == 0 && threadIdx.x == 0) record_status(ri.status, kStatusBadPosition);
+            return;
+        }
+    }
     const int n_ctx = pos + 1 < ctx ? pos + 1 : ctx;
     const int kvh = h / (n_head / n_kv_head);
     const int64_t row_stride = static_cast<int64_t>(n_kv_head) * head_dim;
@@ -292,6 +315,50 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
 
     const int j0 = split * chunk;
     const int j1 = min(n_ctx, j0 + chunk);
+
+    // ROPE: this token's row (slot pos % ctx), when it falls in this chunk
+    constexpr int kNewPer = (HD + kAttnWarps * 32 - 1) / (kAttnWarps * 32);   // elements per thread
+    int new_stage = -1, new_row = 0;
+    __half new_k[kNewPer], new_v[kNewPer];
+    if constexpr (ROPE) {
+        const float* cs = ri.table + static_cast<int64_t>(pos) * HD;
+        // q pieces c and c + QP/2 hold dims d and d + HD/2
+#pragma unroll
+        for (int c = 0; c < QP / 2; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int d = 8 * (4 * c + qq) + i;
+                const float cd = cs[d], sd = cs[HD / 2 + d];
+                const float x0 = qv[c][i], x1 = qv[c + QP / 2][i];
+                qv[c][i] = __fsub_rn(__fmul_rn(x0, cd), __fmul_rn(x1, sd));
+                qv[c + QP / 2][i] = __fadd_rn(__fmul_rn(x0, sd), __fmul_rn(x1, cd));
+            }
+        const int slot = pos % ctx;
+        if (slot >= j0 && slot < j1) {
+            new_stage = (slot - j0) / kAttnStage;
+            new_row = (slot - j0) % kAttnStage;
+            const float* kn = ri.k_new + static_cast<int64_t>(kvh) * HD;
+            const float* vn = ri.v_new + static_cast<int64_t>(kvh) * HD;
+#pragma unroll
+            for (int t = 0; t < kNewPer; ++t) {
+                const int e = threadIdx.x + t * kAttnWarps * 32;   // element e of the row
+                if (e < HD) {
+                    const int d = e < HD / 2 ? e : e - HD / 2;
+                    const float cd = cs[d], sd = cs[HD / 2 + d];
+                    const float x0 = kn[d], x1 = kn[d + HD / 2];
+                    const float r = e < HD / 2 ? __fsub_rn(__fmul_rn(x0, cd), __fmul_rn(x1, sd))
+                                               : __fadd_rn(__fmul_rn(x0, sd), __fmul_rn(x1, cd));
+                    new_k[t] = __float2half_rn(r);
+                    new_v[t] = __float2half_rn(vn[e]);
+                    if (h % (n_head / n_kv_head) == 0) {
+                        const int64_t o = static_cast<int64_t>(slot) * row_stride + static_cast<int64_t>(kvh) * HD + e;
+                        ri.kc[o] = new_k[t];
+                        ri.vc[o] = new_v[t];
+                    }
+                }
+            }
+        }
+    }
     float m = -INFINITY, l = 0.f, acc[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
@@ -326,6 +393,21 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     for (int st = 0; st < n_stage; ++st) {
         cp_async_wait_one();   // stage st has landed (stage st + 1 may still be in flight)
         __syncthreads();
+        if constexpr (ROPE) {
+            if (st == new_stage) {   // CTA-uniform
+                __half* pk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
+                __half* pv = pk + kAttnStage * KS;
+#pragma unroll
+                for (int t = 0; t < kNewPer; ++t) {
+                    const int e = threadIdx.x + t * kAttnWarps * 32;
+                    if (e < HD) {
+                        pk[new_row * KS + e] = new_k[t];
+                        pv[new_row * HD + e] = new_v[t];
+                    }
+                }
+                __syncthreads();
+            }
+        }
         const __half* sk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
         const __half* sv = sk + kAttnStage * KS;
         const int jb = j0 + st * kAttnStage + warp * kAttnPos;   // this warp's first position
@@ -387,6 +469,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     // combine the 4 warps of the CTA
     __shared__ float s_m[kAttnWarps], s_l[kAttnWarps];
     __shared__ float s_acc[kAttnWarps][kAttnMaxDim];
+    __shared__ int s_last;
     if (lane == 0) {
         s_m[warp] = m;
         s_l[warp] = l;
@@ -415,35 +498,54 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
             mine[1] = L;
         }
         __syncwarp();
-        int last = 0;
         if (lane == 0) {
             cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[h]);
-            last = cnt.fetch_add(1, cuda::memory_order_acq_rel) == n_split - 1;
+            s_last = cnt.fetch_add(1, cuda::memory_order_acq_rel) == n_split - 1;
         }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            cuda::atomic_thread_fence(cuda::memory_order_acquire, cuda::thread_scope_device);
-            const float* base = part + static_cast<int64_t>(h) * n_split * (head_dim + 2);
-            // split maxima read by all lanes at once; the weighted sum walks the
-            // splits in order, eight loads in flight at a time
-            float MM = -INFINITY;
-            for (int s2 = lane; s2 < n_split; s2 += 32) MM = fmaxf(MM, base[s2 * (head_dim + 2)]);
+    }
+    __syncthreads();
+    if (s_last) {
+        // the last CTA of the head combines the splits: the maximum over all
+        // of them, then warp w sums splits w, w + 4, ... in order, then the
+        // four warp sums are added in warp order (deterministic)
+        cuda::atomic_thread_fence(cuda::memory_order_acquire, cuda::thread_scope_device);
+        const float* base = part + static_cast<int64_t>(h) * n_split * (head_dim + 2);
+        float MM = -INFINITY;
+        for (int s2 = threadIdx.x; s2 < n_split; s2 += blockDim.x) MM = fmaxf(MM, base[s2 * (head_dim + 2)]);
 #pragma unroll
-            for (int o2 = 16; o2 > 0; o2 >>= 1) MM = fmaxf(MM, __shfl_xor_sync(0xffffffffu, MM, o2));
-            float LL = 0.f, o[DPL];
+        for (int o2 = 16; o2 > 0; o2 >>= 1) MM = fmaxf(MM, __shfl_xor_sync(0xffffffffu, MM, o2));
+        if (lane == 0) s_m[warp] = MM;
+        __syncthreads();
+        MM = s_m[0];
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) o[i] = 0.f;
-#pragma unroll 8
-            for (int s2 = 0; s2 < n_split; ++s2) {
-                const float* p = base + s2 * (head_dim + 2);
-                const float f = p[0] == -INFINITY ? 0.f : expf(p[0] - MM);
-                LL = fmaf(p[1], f, LL);
+        for (int w = 1; w < kAttnWarps; ++w) MM = fmaxf(MM, s_m[w]);
+        float LL = 0.f, o[DPL];
 #pragma unroll
-                for (int i = 0; i < DPL; ++i) o[i] = fmaf(p[2 + lane * DPL + i], f, o[i]);
+        for (int i = 0; i < DPL; ++i) o[i] = 0.f;
+#pragma unroll 4
+        for (int s2 = warp; s2 < n_split; s2 += kAttnWarps) {
+            const float* p = base + s2 * (head_dim + 2);
+            const float f = p[0] == -INFINITY ? 0.f : expf(p[0] - MM);
+            LL = fmaf(p[1], f, LL);
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) o[i] = fmaf(p[2 + lane * DPL + i], f, o[i]);
+        }
+        if (lane == 0) s_l[warp] = LL;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) s_acc[warp][lane * DPL + i] = o[i];
+        __syncthreads();
+        if (warp == 0) {
+            float L = s_l[0];
+#pragma unroll
+            for (int w = 1; w < kAttnWarps; ++w) L += s_l[w];
+            const float inv = 1.0f / L;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) {
+                float a = s_acc[0][lane * DPL + i];
+#pragma unroll
+                for (int w = 1; w < kAttnWarps; ++w) a += s_acc[w][lane * DPL + i];
+                out[static_cast<int64_t>(h) * head_dim + lane * DPL + i] = a * inv;
             }
-            const float inv = 1.0f / LL;
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) out[static_cast<int64_t>(h) * head_dim + lane * DPL + i] = o[i] * inv;
             if (lane == 0) {
                 cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[h]);
                 cnt.store(0, cuda::memory_order_relaxed);
@@ -540,10 +642,10 @@ int attention_splits(int64_t ctx) {
     return static_cast<int>(n);
 }
 
-template <int DPL>
+template <int DPL, bool ROPE>
 cudaError_t launch_attention(dim3 grid, size_t smem, cudaStream_t s, const float* q, const __half* k, const __half* v,
                              float* out, int nh, int nkv, int c, const int32_t* pos_dev, int32_t pos_host, int chunk,
-                             float* part, int* counters) {
+                             float* part, int* counters, const AttnRope& ri) {
     if (smem > 48 * 1024) {
         static int set[64] = {0};
         int dev = 0;
@@ -551,20 +653,21 @@ cudaError_t launch_attention(dim3 grid, size_t smem, cudaStream_t s, const float
         if (e != cudaSuccess) return e;
         if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
         if (set[dev] < static_cast<int>(smem)) {
-            e = cudaFuncSetAttribute(attention_kernel<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            e = cudaFuncSetAttribute(attention_kernel<DPL, ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem));
             if (e != cudaSuccess) return e;
             set[dev] = static_cast<int>(smem);
         }
     }
-    attention_kernel<DPL><<<grid, kAttnWarps * 32, smem, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk,
-                                                               part, counters);
+    attention_kernel<DPL, ROPE><<<grid, kAttnWarps * 32, smem, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host,
+                                                                     chunk, part, counters, ri);
     return cudaGetLastError();
 }
 
-cudaError_t attention(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,
-                      int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
-                      void* workspace, cudaStream_t s) {
+template <bool ROPE>
+cudaError_t attention_any(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,
+                          int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
+                          void* workspace, const AttnRope& ri, cudaStream_t s) {
     const int n_split = attention_splits(ctx);
     const int chunk = static_cast<int>((ctx + n_split - 1) / n_split);
     int* counters = static_cast<int*>(workspace);
@@ -576,14 +679,36 @@ cudaError_t attention(const float* q, const void* kc, const void* vc, float* out
     const int nh = static_cast<int>(n_head), nkv = static_cast<int>(n_kv_head), c = static_cast<int>(ctx);
     // two stage buffers of K (rows padded by 16 bytes) and V
     const size_t smem = static_cast<size_t>(2 * kAttnStage) * static_cast<size_t>(2 * head_dim + 8) * 2;
-    cudaError_t e = cudaSuccess;
     switch (head_dim) {
-        case 64: e = launch_attention<2>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
-        case 128: e = launch_attention<4>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
-        case 256: e = launch_attention<8>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part, counters); break;
+        case 64:
+            return launch_attention<2, ROPE>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part,
+                                             counters, ri);
+        case 128:
+            return launch_attention<4, ROPE>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part,
+                                             counters, ri);
+        case 256:
+            return launch_attention<8, ROPE>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part,
+                                             counters, ri);
         default: return cudaErrorInvalidValue;
     }
-    return e;
+}
+
+cudaError_t attention(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,
+                      int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
+                      void* workspace, cudaStream_t s) {
+    return attention_any<false>(q, kc, vc, out, n_head, n_kv_head, head_dim, ctx, pos_dev, pos_host, workspace,
+                                AttnRope{}, s);
+}
+
+cudaError_t attention_rope(const float* q, const float* k_new, const float* v_new, void* kc, void* vc, float* out,
+                           int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
+                           int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
+                           cudaStream_t s) {
+    int* status = nullptr;
+    cudaError_t e = status_word(&status);
+    if (e != cudaSuccess) return e;
+    const AttnRope ri = {k_new, v_new, static_cast<__half*>(kc), static_cast<__half*>(vc), table, table_rows, status};
+    return attention_any<true>(q, kc, vc, out, n_head, n_kv_head, head_dim, ctx, pos_dev, 0, workspace, ri, s);
 }
 
 }  // namespace hesa_cuda

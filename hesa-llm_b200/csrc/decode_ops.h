@@ -28,5 +28,13 @@ size_t attention_workspace_bytes(int64_t n_head, int64_t head_dim, int64_t ctx);
 cudaError_t attention(const float* q, const void* kc, const void* vc, float* out, int64_t n_head,
                       int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
                       void* workspace, cudaStream_t s);
+// rope_kv followed by attention in one launch (the decode step's form): q and
+// k_new unrotated, this token's k and v written to slot *pos_dev % ctx; a
+// position outside the rope table records device status 3 and computes
+// nothing.
+cudaError_t attention_rope(const float* q, const float* k_new, const float* v_new, void* kc, void* vc, float* out,
+                           int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
+                           int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
+                           cudaStream_t s);
 
 }  // namespace hesa_cuda

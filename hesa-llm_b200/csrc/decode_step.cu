@@ -199,13 +199,26 @@ int hesa_cuda_decode_step(const hesa_cuda_model* m, const hesa_cuda_layer* layer
                 if (!rc) rc = mv(Ly.wv, KD, D, h, v);
             }
         }
-        if (!rc) {
-            const cudaError_t e = hesa_cuda::rope_kv(q, k, v, Ly.k_cache, Ly.v_cache, NH, NKV, HD, rope_table,
-                                                     rope_rows, m->ctx, pos_dev, s);
-            if (e != cudaSuccess) rc = hesa_cuda::record_cuda_error(e, "rope + KV write");
+        const bool att_fused = (reinterpret_cast<uintptr_t>(Ly.k_cache) & 15) == 0 &&
+                               (reinterpret_cast<uintptr_t>(Ly.v_cache) & 15) == 0 &&
+                               (HD == 64 || HD == 128 || HD == 256) && m->ctx <= 131072 &&
+                               L.att_bytes >= hesa_cuda::attention_workspace_bytes(NH, HD, m->ctx);
+        if (att_fused) {
+            // rope, KV write and attention in one launch
+            if (!rc) {
+                const cudaError_t e = hesa_cuda::attention_rope(q, k, v, Ly.k_cache, Ly.v_cache, a, NH, NKV, HD,
+                                                                rope_table, rope_rows, m->ctx, pos_dev, att_ws, s);
+                if (e != cudaSuccess) rc = hesa_cuda::record_cuda_error(e, "attention with rope + KV write");
+            }
+        } else {
+            if (!rc) {
+                const cudaError_t e = hesa_cuda::rope_kv(q, k, v, Ly.k_cache, Ly.v_cache, NH, NKV, HD, rope_table,
+                                                         rope_rows, m->ctx, pos_dev, s);
+                if (e != cudaSuccess) rc = hesa_cuda::record_cuda_error(e, "rope + KV write");
+            }
+            if (!rc) rc = hesa_cuda_attention(q, Ly.k_cache, Ly.v_cache, a, NH, NKV, HD, m->ctx, pos_dev, 0, att_ws,
+                                              L.att_bytes, stream);
         }
-        if (!rc) rc = hesa_cuda_attention(q, Ly.k_cache, Ly.v_cache, a, NH, NKV, HD, m->ctx, pos_dev, 0, att_ws,
-                                          L.att_bytes, stream);
         if (fusable(Ly.wo, D, QD, StripInput::kPlain)) {
             if (!rc) rc = fmv(Ly.wo, D, QD, a, StripInput::kPlain, nullptr, x, x);
         } else {
