@@ -66,6 +66,24 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
+// L2 policy for data read once (streamed weights): its lines are the first
+// to be evicted, so the stream does not push activations, KV rows or the
+// next kernel's inputs out of L2.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// bulk_g2s with an L2 cache policy for the source lines.
+__device__ __forceinline__ void bulk_g2s_policy(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                                uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(smem_addr(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 // 2-D tiled tensor copy (TMA) of the box at element coordinates (x, y) of the
 // tensor map into shared memory, completing on `bar`. No cluster multicast.
 __device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tensor_map, int x, int y, uint64_t* bar) {

@@ -750,7 +750,9 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         }
         issued[slot] = j;
         mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(a1 - a0));
-        if (a1 > a0) bulk_g2s(dst, w + a0, static_cast<uint32_t>(a1 - a0), &full[slot]);
+        // each weight byte is read once: evict-first in L2 (sweep 3,010 -> 3,080 GB/s)
+        if (a1 > a0)
+            bulk_g2s_policy(dst, w + a0, static_cast<uint32_t>(a1 - a0), &full[slot], l2_policy_evict_first());
     };
 
     // The weights never come from the previous kernel on the stream, so the
