@@ -307,14 +307,53 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     const float sc = 1.0f / sqrtf(static_cast<float>(head_dim));
 
     const int t8 = lane >> 2, qq = lane & 3;   // scoring: position t8 of the step, piece phase qq
+    const int j0 = split * chunk;
+    const int j1 = min(n_ctx, j0 + chunk);
+
+    float m = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+
+    // The chunk streams through shared memory in stages of kAttnStage
+    // positions, two buffers deep: the cp.async copies of stage s + 2 are in
+    // flight while stage s is computed (16-byte pieces, every thread issuing
+    // its share). Each warp takes kAttnPos positions of every stage: the score
+    // reductions interleave and the running softmax is rescaled once per step.
+    extern __shared__ __align__(16) uint8_t attn_smem[];
+    __half* sbuf = reinterpret_cast<__half*>(attn_smem);   // [2][K (padded rows) | V][kAttnStage]
+    constexpr int kPieces = DPL * 32 * 2 / 16;               // 16-byte pieces per row
+    const int rows = j1 > j0 ? j1 - j0 : 0;
+    const int n_stage = (rows + kAttnStage - 1) / kAttnStage;
+    const __half* kg = kc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
+    const __half* vg = vc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
+    auto issue = [&](int st) {
+        if (st < n_stage) {
+            __half* sk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
+            __half* sv = sk + kAttnStage * KS;
+            const int r0 = st * kAttnStage, nr = min(kAttnStage, rows - r0);
+            for (int c = threadIdx.x; c < nr * kPieces; c += blockDim.x) {
+                const int r = c / kPieces, o = (c - r * kPieces) * 8;
+                cp_async16(sk + r * KS + o, kg + static_cast<int64_t>(r0 + r) * row_stride + o);
+                cp_async16(sv + r * head_dim + o, vg + static_cast<int64_t>(r0 + r) * row_stride + o);
+            }
+        }
+        cp_async_commit();   // an empty group when there is no such stage
+    };
+    // With ROPE (the decode step, launched with programmatic stream
+    // serialization) the first two stages are requested before waiting for the
+    // previous kernel: the cache rows of earlier tokens are never written by it
+    // (this token's row is patched in below); q, k and v are, so they are read
+    // after the wait.
+    if constexpr (ROPE) {
+        issue(0);
+        issue(1);
+        grid_dep_wait();
+    }
     float qv[QP][8];
 #pragma unroll
     for (int c = 0; c < QP; ++c)
 #pragma unroll
         for (int i = 0; i < 8; ++i) qv[c][i] = q[static_cast<int64_t>(h) * HD + 8 * (4 * c + qq) + i];
-
-    const int j0 = split * chunk;
-    const int j1 = min(n_ctx, j0 + chunk);
 
     // ROPE: this token's row (slot pos % ctx), when it falls in this chunk
     constexpr int kNewPer = (HD + kAttnWarps * 32 - 1) / (kAttnWarps * 32);   // elements per thread
@@ -359,37 +398,10 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
             }
         }
     }
-    float m = -INFINITY, l = 0.f, acc[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-
-    // The chunk streams through shared memory in stages of kAttnStage
-    // positions, two buffers deep: the cp.async copies of stage s + 2 are in
-    // flight while stage s is computed (16-byte pieces, every thread issuing
-    // its share). Each warp takes kAttnPos positions of every stage: the score
-    // reductions interleave and the running softmax is rescaled once per step.
-    extern __shared__ __align__(16) uint8_t attn_smem[];
-    __half* sbuf = reinterpret_cast<__half*>(attn_smem);   // [2][K (padded rows) | V][kAttnStage]
-    constexpr int kPieces = DPL * 32 * 2 / 16;               // 16-byte pieces per row
-    const int rows = j1 > j0 ? j1 - j0 : 0;
-    const int n_stage = (rows + kAttnStage - 1) / kAttnStage;
-    const __half* kg = kc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
-    const __half* vg = vc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
-    auto issue = [&](int st) {
-        if (st < n_stage) {
-            __half* sk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
-            __half* sv = sk + kAttnStage * KS;
-            const int r0 = st * kAttnStage, nr = min(kAttnStage, rows - r0);
-            for (int c = threadIdx.x; c < nr * kPieces; c += blockDim.x) {
-                const int r = c / kPieces, o = (c - r * kPieces) * 8;
-                cp_async16(sk + r * KS + o, kg + static_cast<int64_t>(r0 + r) * row_stride + o);
-                cp_async16(sv + r * head_dim + o, vg + static_cast<int64_t>(r0 + r) * row_stride + o);
-            }
-        }
-        cp_async_commit();   // an empty group when there is no such stage
-    };
-    issue(0);
-    issue(1);
+    if constexpr (!ROPE) {
+        issue(0);
+        issue(1);
+    }
     for (int st = 0; st < n_stage; ++st) {
         cp_async_wait_one();   // stage st has landed (stage st + 1 may still be in flight)
         __syncthreads();
@@ -465,6 +477,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
         issue(st + 2);
     }
     cp_async_wait_all();   // nothing left in flight (the trailing groups are empty)
+    if constexpr (ROPE) grid_dep_launch();   // the next launch may take the SMs this grid leaves
 
     // combine the 4 warps of the CTA
     __shared__ float s_m[kAttnWarps], s_l[kAttnWarps];
@@ -505,45 +518,50 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     }
     __syncthreads();
     if (s_last) {
-        // the last CTA of the head combines the splits: the maximum over all
-        // of them, then warp w sums splits w, w + 4, ... in order, then the
-        // four warp sums are added in warp order (deterministic)
+        // the last CTA of the head combines the splits in one pass over them:
+        // warp w folds splits w, w + 4, ... into a running (max, sum, acc),
+        // rescaling as the maximum grows; the four warp results are then
+        // merged in warp order (deterministic)
         cuda::atomic_thread_fence(cuda::memory_order_acquire, cuda::thread_scope_device);
         const float* base = part + static_cast<int64_t>(h) * n_split * (head_dim + 2);
-        float MM = -INFINITY;
-        for (int s2 = threadIdx.x; s2 < n_split; s2 += blockDim.x) MM = fmaxf(MM, base[s2 * (head_dim + 2)]);
-#pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) MM = fmaxf(MM, __shfl_xor_sync(0xffffffffu, MM, o2));
-        if (lane == 0) s_m[warp] = MM;
-        __syncthreads();
-        MM = s_m[0];
-#pragma unroll
-        for (int w = 1; w < kAttnWarps; ++w) MM = fmaxf(MM, s_m[w]);
-        float LL = 0.f, o[DPL];
+        float Mw = -INFINITY, LL = 0.f, o[DPL];
 #pragma unroll
         for (int i = 0; i < DPL; ++i) o[i] = 0.f;
 #pragma unroll 4
         for (int s2 = warp; s2 < n_split; s2 += kAttnWarps) {
             const float* p = base + s2 * (head_dim + 2);
-            const float f = p[0] == -INFINITY ? 0.f : expf(p[0] - MM);
-            LL = fmaf(p[1], f, LL);
+            const float ms = p[0];
+            const float mn = fmaxf(Mw, ms);
+            const float fo = Mw == -INFINITY ? 0.f : expf(Mw - mn);
+            const float fs = ms == -INFINITY ? 0.f : expf(ms - mn);
+            LL = fmaf(p[1], fs, LL * fo);
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) o[i] = fmaf(p[2 + lane * DPL + i], f, o[i]);
+            for (int i = 0; i < DPL; ++i) o[i] = fmaf(p[2 + lane * DPL + i], fs, o[i] * fo);
+            Mw = mn;
         }
-        if (lane == 0) s_l[warp] = LL;
+        if (lane == 0) {
+            s_m[warp] = Mw;
+            s_l[warp] = LL;
+        }
 #pragma unroll
         for (int i = 0; i < DPL; ++i) s_acc[warp][lane * DPL + i] = o[i];
         __syncthreads();
         if (warp == 0) {
-            float L = s_l[0];
+            float M = s_m[0];
 #pragma unroll
-            for (int w = 1; w < kAttnWarps; ++w) L += s_l[w];
+            for (int w = 1; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w]);
+            float f[kAttnWarps];
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; ++w) f[w] = s_m[w] == -INFINITY ? 0.f : expf(s_m[w] - M);
+            float L = 0.f;
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; ++w) L = fmaf(s_l[w], f[w], L);
             const float inv = 1.0f / L;
 #pragma unroll
             for (int i = 0; i < DPL; ++i) {
-                float a = s_acc[0][lane * DPL + i];
+                float a = 0.f;
 #pragma unroll
-                for (int w = 1; w < kAttnWarps; ++w) a += s_acc[w][lane * DPL + i];
+                for (int w = 0; w < kAttnWarps; ++w) a = fmaf(s_acc[w][lane * DPL + i], f[w], a);
                 out[static_cast<int64_t>(h) * head_dim + lane * DPL + i] = a * inv;
             }
             if (lane == 0) {
@@ -659,9 +677,26 @@ cudaError_t launch_attention(dim3 grid, size_t smem, cudaStream_t s, const float
             set[dev] = static_cast<int>(smem);
         }
     }
-    attention_kernel<DPL, ROPE><<<grid, kAttnWarps * 32, smem, s>>>(q, k, v, out, nh, nkv, c, pos_dev, pos_host,
-                                                                     chunk, part, counters, ri);
-    return cudaGetLastError();
+    if constexpr (!ROPE) {
+        attention_kernel<DPL, ROPE><<<grid, kAttnWarps * 32, smem, s>>>(q, k, v, out, nh, nkv, c, pos_dev,
+                                                                         pos_host, chunk, part, counters, ri);
+        return cudaGetLastError();
+    } else {
+        // programmatic stream serialization: the CTAs may start while the
+        // previous kernel finishes; the kernel waits for it before reading q, k, v
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kAttnWarps * 32);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, attention_kernel<DPL, ROPE>, q, k, v, out, nh, nkv, c, pos_dev, pos_host,
+                                  chunk, part, counters, ri);
+    }
 }
 
 template <bool ROPE>
