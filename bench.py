@@ -370,6 +370,60 @@ def run_batched(dev, stream, reps: int = 20):
     return out
 
 
+PROJ70B = (("wq", 8192, 8192), ("wk", 1024, 8192), ("wv", 1024, 8192), ("wo", 8192, 8192),
+           ("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672))
+
+
+def proj70b_bytes(world: int) -> int:
+    """Algorithmic bytes of one pass over the 70B projection set, all ranks
+    together: every packed row once, x once per rank, every output once."""
+    qt = QT["Q4_K"]
+    return sum(n * row_bytes(qt, k) + 4 * k * world + 4 * n for _, n, k in PROJ70B)
+
+
+def run_proj70b(dev, stream, rank: int, world: int, reps: int = 20):
+    """70B-shaped Q4_K projections (d_model 8192, FFN 28672, 8 KV heads of
+    128), batch 1, row-sharded: this rank holds rows [r0, r1) of each of the
+    seven matrices (sharding.row_range) and one pass is its seven matvecs,
+    replayed from a CUDA graph (443 MB of weights at N = 1, more than L2).
+    Returns ms per pass on this rank (device time)."""
+    import torch
+    import hesa_cuda as H
+    import sharding
+    qt = QT["Q4_K"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(7070 + rank)
+    mats = []
+    for name, n, k in PROJ70B:
+        r0, r1 = sharding.row_range(n, rank, world)
+        w = H.quantize(qt, torch.randn((r1 - r0, k), generator=g, device=dev) * 0.02)
+        x = torch.randn(k, generator=g, device=dev)
+        y = torch.empty(r1 - r0, device=dev)
+        mats.append((w, x, y, H.make_workspace(qt, r1 - r0, k, device=dev)))
+    with torch.cuda.stream(stream):
+        def one():
+            for w, x, y, ws in mats:
+                H.qmatvec(qt, w, x, y=y, workspace=ws, stream=stream)
+        one()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            one()
+        for _ in range(3):
+            graph.replay()
+        stream.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del graph, mats
+    return ms
+
+
 def run_decode(dev, stream, steps: int, warmup: int, pg=None):
     """tokens/s of the 7B-shaped Q4_K decode step (embedding lookup + every
     layer + LM head), one CUDA graph per token, device-timed."""
@@ -735,13 +789,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     # the 7B-shaped Q4_K decode step, one full replica per rank
     dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg)
     batched = run_batched(dev, stream) if rank == 0 else None
+    p70_ms = run_proj70b(dev, stream, rank, world)
 
     # max over ranks
     times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec["ms"], nccl_ms or 0.0,
-                          0.0 if peers is None or gathered_ok else 1.0], dtype=torch.float64, device=dev)
+                          0.0 if peers is None or gathered_ok else 1.0, p70_ms], dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
-    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms, nccl_ms, gather_bad = (float(v) for v in times.cpu())
+    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms, nccl_ms, gather_bad, p70_ms = (float(v) for v in times.cpu())
 
     if rank == 0:
         bytes_step = step_bytes() * world
@@ -801,6 +856,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                     "one launch per 16 rows on the tensor cores (B >= 2)",
                         "us_and_gbs": batched,
                         "timing": "8 rotating weight copies (203 MB > L2) in one CUDA graph, CUDA events, rank 0"},
+            "proj70b": {"workload": "70B-shaped Q4_K projections, batch 1: Wq, Wo 8192x8192; Wk, Wv 1024x8192; "
+                                   "gate, up 28672x8192; down 8192x28672 ([n_out x k])",
+                        "parallelism": (f"rows split over {world} GPUs (each rank its shards; time = max over "
+                                        "ranks; outputs stay on their rank, the fused gather is timed in the "
+                                        "sweep line)" if world > 1 else "single GPU"),
+                        "scaling": "strong",
+                        "ms_per_pass": round(p70_ms, 4),
+                        "gbs": round(proj70b_bytes(world) / (p70_ms * 1e-3) / 1e9, 1),
+                        "bytes_per_pass": proj70b_bytes(world),
+                        "timing": "the seven matvecs in one CUDA graph, 20 replays between CUDA events"},
             "clocks": clocks,
             "cpu_baseline": cpu_base,
         }
