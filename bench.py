@@ -42,8 +42,26 @@ import time
 
 import numpy as np
 
-# NCCL's informational lines go to stdout, which carries the one JSON line
+# stdout carries the one JSON line. NCCL writes its log (the version banner
+# included, at every level but NONE) to stdout; the line goes out through a
+# duplicate of the original stdout (RESULT) and file descriptor 1 is pointed at
+# stderr, so whatever a library prints lands there.
 os.environ.setdefault("NCCL_DEBUG", "WARN")
+RESULT = None
+
+
+def _route_stdout():
+    global RESULT
+    if RESULT is None:
+        sys.stdout.flush()
+        RESULT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(obj) -> None:
+    """Print the bench's JSON line on the original stdout."""
+    out = RESULT if RESULT is not None else sys.stdout
+    print(json.dumps(obj), file=out, flush=True)
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "hesa-llm_b200")
@@ -249,7 +267,7 @@ def run_reference(args, rank: int, world: int):
     budget = max(0.05, 120.0 / max(args.steps, 1))
     base = cpu_reference_rate(mats, max_pass_seconds=budget, passes=args.steps)
     if base is None:
-        print(json.dumps({"impl": "reference", "unavailable": "reference CPU library (oracle/_ref) not built"}))
+        emit({"impl": "reference", "unavailable": "reference CPU library (oracle/_ref) not built"})
         return 0
     per_step_ms = base["seconds"] / args.steps * 1e3
     out = {"metric": METRIC, "value": round(base["value"], 3), "unit": "GB/s", "impl": "reference",
@@ -261,7 +279,7 @@ def run_reference(args, rank: int, world: int):
            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
            "e2e": {"value": round(base["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
-    print(json.dumps(out), flush=True)
+    emit(out)
     return 0
 
 
@@ -869,7 +887,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             "clocks": clocks,
             "cpu_baseline": cpu_base,
         }
-        print(json.dumps(out), flush=True)
+        emit(out)
 
     del graph, g_e2e   # graphs that hold NCCL calls go before the process group
     if pg is not None:
@@ -883,6 +901,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
 
 def main():
+    _route_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)

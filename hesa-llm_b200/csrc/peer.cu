@@ -2,10 +2,11 @@
 // matvecs (see PeerOut in qmatvec.h).
 //
 // The strip kernels of a step store their rows into every rank's gathered
-// buffer over NVLink and end with a system-scope fence. The barrier then runs
-// on each rank's stream: lane p publishes the step number into slot `rank` of
-// rank p's flag array (st.release.sys) and waits until slot p of this rank's
-// own array carries it (ld.acquire.sys). When every lane has seen its peer, all
+// buffer over NVLink; the barrier kernel is launched after them without
+// programmatic serialization, so it starts once their grids (and stores)
+// have completed. On each rank's stream, lane p then publishes the step
+// number into slot `rank` of rank p's flag array (st.release.sys) and waits
+// until slot p of this rank's own array carries it (ld.acquire.sys). When every lane has seen its peer, all
 // ranks have finished storing this step's rows here. Plain peer loads and
 // stores only: no multimem, no multicast object.
 #include "hesa_common.cuh"
@@ -40,6 +41,7 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int* __re
     const uint32_t e = *f.epoch + 1u;
     __syncwarp();
     if (t < f.world) {
+        __threadfence_system();
         st_release_sys(f.flags[t] + f.rank, e);
         const uint32_t* mine = f.flags[f.rank] + t;
         if (!reached(mine, e)) {
