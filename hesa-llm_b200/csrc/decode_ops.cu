@@ -213,6 +213,7 @@ constexpr int kAttnMaxDim = 256;
 constexpr int kAttnPos = 8;   // positions per warp step
 constexpr int kAttnMaxSplits = 1024;
 constexpr int kAttnStage = 32;   // positions per pipeline stage: kAttnWarps warps x kAttnPos
+constexpr int kAttnDepth = 3;    // stage buffers: three stages in flight (4 CTAs per SM at head_dim 128)
 static_assert(kAttnStage == kAttnWarps * kAttnPos, "a stage is one step of every warp");
 
 // DPL consecutive fp16 values (2, 4 or 8: one 4-, 8- or 16-byte load).
@@ -242,8 +243,10 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
                  ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))), "l"(gmem_src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// wait until at most one committed group of this thread is still in flight
-__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+// wait until at most kAttnDepth - 1 committed groups of this thread are still in flight
+__device__ __forceinline__ void cp_async_wait_depth() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kAttnDepth - 1) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 template <int DPL>
@@ -315,12 +318,12 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
 
     // The chunk streams through shared memory in stages of kAttnStage
-    // positions, two buffers deep: the cp.async copies of stage s + 2 are in
-    // flight while stage s is computed (16-byte pieces, every thread issuing
+    // positions, kAttnDepth buffers deep: the cp.async copies of stages s + 1
+    // and s + 2 are in flight while stage s is computed (16-byte pieces, every thread issuing
     // its share). Each warp takes kAttnPos positions of every stage: the score
     // reductions interleave and the running softmax is rescaled once per step.
     extern __shared__ __align__(16) uint8_t attn_smem[];
-    __half* sbuf = reinterpret_cast<__half*>(attn_smem);   // [2][K (padded rows) | V][kAttnStage]
+    __half* sbuf = reinterpret_cast<__half*>(attn_smem);   // [kAttnDepth][K (padded rows) | V][kAttnStage]
     constexpr int kPieces = DPL * 32 * 2 / 16;               // 16-byte pieces per row
     const int rows = j1 > j0 ? j1 - j0 : 0;
     const int n_stage = (rows + kAttnStage - 1) / kAttnStage;
@@ -328,7 +331,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     const __half* vg = vc + static_cast<int64_t>(j0) * row_stride + static_cast<int64_t>(kvh) * head_dim;
     auto issue = [&](int st) {
         if (st < n_stage) {
-            __half* sk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
+            __half* sk = sbuf + static_cast<int64_t>(st % kAttnDepth) * kAttnStage * (KS + HD);
             __half* sv = sk + kAttnStage * KS;
             const int r0 = st * kAttnStage, nr = min(kAttnStage, rows - r0);
             for (int c = threadIdx.x; c < nr * kPieces; c += blockDim.x) {
@@ -347,6 +350,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     if constexpr (ROPE) {
         issue(0);
         issue(1);
+        issue(2);
         grid_dep_wait();
     }
     float qv[QP][8];
@@ -401,13 +405,14 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
     if constexpr (!ROPE) {
         issue(0);
         issue(1);
+        issue(2);
     }
     for (int st = 0; st < n_stage; ++st) {
-        cp_async_wait_one();   // stage st has landed (stage st + 1 may still be in flight)
+        cp_async_wait_depth();   // stage st has landed (stages st + 1, st + 2 may still be in flight)
         __syncthreads();
         if constexpr (ROPE) {
             if (st == new_stage) {   // CTA-uniform
-                __half* pk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
+                __half* pk = sbuf + static_cast<int64_t>(st % kAttnDepth) * kAttnStage * (KS + HD);
                 __half* pv = pk + kAttnStage * KS;
 #pragma unroll
                 for (int t = 0; t < kNewPer; ++t) {
@@ -420,7 +425,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
                 __syncthreads();
             }
         }
-        const __half* sk = sbuf + static_cast<int64_t>(st & 1) * kAttnStage * (KS + HD);
+        const __half* sk = sbuf + static_cast<int64_t>(st % kAttnDepth) * kAttnStage * (KS + HD);
         const __half* sv = sk + kAttnStage * KS;
         const int jb = j0 + st * kAttnStage + warp * kAttnPos;   // this warp's first position
         if (jb < j1) {
@@ -474,7 +479,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
             m = mx;
         }
         __syncthreads();   // every warp is done with this buffer before it is refilled
-        issue(st + 2);
+        issue(st + kAttnDepth);
     }
     cp_async_wait_all();   // nothing left in flight (the trailing groups are empty)
     if constexpr (ROPE) grid_dep_launch();   // the next launch may take the SMs this grid leaves
@@ -712,8 +717,8 @@ cudaError_t attention_any(const float* q, const void* kc, const void* vc, float*
     const __half* k = static_cast<const __half*>(kc);
     const __half* v = static_cast<const __half*>(vc);
     const int nh = static_cast<int>(n_head), nkv = static_cast<int>(n_kv_head), c = static_cast<int>(ctx);
-    // two stage buffers of K (rows padded by 16 bytes) and V
-    const size_t smem = static_cast<size_t>(2 * kAttnStage) * static_cast<size_t>(2 * head_dim + 8) * 2;
+    // kAttnDepth stage buffers of K (rows padded by 16 bytes) and V
+    const size_t smem = static_cast<size_t>(kAttnDepth * kAttnStage) * static_cast<size_t>(2 * head_dim + 8) * 2;
     switch (head_dim) {
         case 64:
             return launch_attention<2, ROPE>(grid, smem, s, q, k, v, out, nh, nkv, c, pos_dev, pos_host, chunk, part,
