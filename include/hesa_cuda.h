@@ -302,7 +302,10 @@ HESA_CUDA_API int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_r
                                            float scale, float* const* y_peers, int world, const uint32_t* epoch,
                                            void* stream);
 
-/* End of a step of gathered matvecs: publishes *epoch + 1 into slot `rank`
+/* End of a step of gathered matvecs (enqueue it on the stream of those
+ * matvecs: it starts after their grids have completed, which is what makes
+ * their peer stores visible; it then fences at system scope): publishes
+ * *epoch + 1 into slot `rank`
  * of every rank's flag array (flags: host array of `world` device pointers to
  * uint32[world], flags[p] = rank p's array as mapped here, flags[rank] this
  * rank's own), waits until every slot of this rank's array holds it, then
