@@ -1,7 +1,7 @@
 /*
  * hesa_oracle.c -- CPU restatement of the GGUF quantized matvec path.
  *
- * TEST INFRASTRUCTURE ONLY (the checker). See hesa_oracle.h for what each
+ * TEST INFRASTRUCTURE ONLY (the oracle the parity tests compare against). See hesa_oracle.h for what each
  * function restates and where its semantics come from. Compiled with
  * -O2 -ffp-contract=off (-fopenmp for the row-parallel loops).
  */

@@ -1,7 +1,7 @@
 /*
  * hesa_oracle.h -- CPU restatement of the GGUF block-quantized matvec path.
  *
- * TEST INFRASTRUCTURE ONLY. This library is the checker: the parity tests,
+ * TEST INFRASTRUCTURE ONLY. This library is the oracle: the parity tests,
  * smoke() and bench.py's CPU-baseline leg call it to produce expected values.
  * No product code path may link, load or call it.
  *

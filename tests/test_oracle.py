@@ -1,5 +1,5 @@
 """CPU tests: the oracle against the committed golden fixtures and the
-reference's own known answers. These pin the checker before any GPU result is
+reference's own known answers. These pin the oracle before any GPU result is
 compared with it."""
 import os
 

@@ -1,7 +1,7 @@
 """GPU parity of the CUDA matvec and dequantizer against the oracle, through
 the C ABI (hesa_cuda -> libhesa_cuda.so).
 
-Bars (north star of this backend): dequantized weights bit-exact; matvec
+Bars: dequantized weights bit-exact; matvec
 outputs within relative L2 error REL_L2_TOL of the fp32 oracle."""
 import os
 
