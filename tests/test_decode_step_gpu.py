@@ -20,8 +20,8 @@ def rel_l2(a, b):
     return float(np.linalg.norm(np.asarray(a, np.float64) - b) / np.linalg.norm(b))
 
 
-def build_model(qt, seed=7, prefill=40):
-    c = dict(CFG, qtype=qt)
+def build_model(qt, seed=7, prefill=40, cfg=None):
+    c = dict(cfg or CFG, qtype=qt)
     D, QD, KD, F, V = c["d_model"], c["n_head"] * c["head_dim"], c["n_kv_head"] * c["head_dim"], c["d_ff"], c["vocab"]
     layers = []
     for l in range(c["n_layer"]):
@@ -43,7 +43,7 @@ def build_model(qt, seed=7, prefill=40):
     return c, layers, out_norm, w_out, emb
 
 
-def to_device(c, layers, out_norm, w_out, joined):
+def to_device(c, layers, out_norm, w_out, joined, rope_rows=ROPE_ROWS):
     import torch
     import hesa_cuda as H
     dev = "cuda"
@@ -68,7 +68,7 @@ def to_device(c, layers, out_norm, w_out, joined):
         per.append(d)
     m = H.Model(c["n_layer"], c["d_model"], c["n_head"], c["n_kv_head"], c["head_dim"], c["d_ff"], c["vocab"],
                 c["ctx"], c["rms_eps"], c["rope_base"], c["qtype"])
-    table = torch.from_numpy(H.rope_table(ROPE_ROWS, c["head_dim"], c["rope_base"])).to(dev)
+    table = torch.from_numpy(H.rope_table(rope_rows, c["head_dim"], c["rope_base"])).to(dev)
     return dict(model=m, per=per, keep=keep, layers=H.make_layers(per), out_norm=torch.from_numpy(out_norm).to(dev),
                 w_out=torch.from_numpy(w_out).to(dev), table=table, ws=H.decode_workspace(m),
                 logits=torch.empty(c["vocab"], dtype=torch.float32, device=dev))
@@ -113,6 +113,35 @@ def test_decode_step_matches_oracle(qt, joined):
         assert err <= 1e-5, f"step {step} pos {pos}: rel L2 {err:.3e}"
         check_caches(c, g, layers, pos)
         # continue from the oracle's caches so both sides carry identical state
+        for d, w in zip(g["per"], layers):
+            for n in ("k_cache", "v_cache"):
+                d[n].copy_(torch.from_numpy(w[n].view(np.int16)))
+    assert H.device_status() == 0
+
+
+# head_dim 128 (the 7B shape's) with four query heads per KV head and a context
+# of four 128-slot splits; the last position wraps the ring
+CFG_HD128 = dict(n_layer=2, d_model=512, n_head=8, n_kv_head=2, head_dim=128, d_ff=1024, vocab=512, ctx=512,
+                 rms_eps=1e-6, rope_base=10000.0)
+
+
+def test_decode_step_head_dim_128_gqa_matches_oracle():
+    import torch
+    import hesa_cuda as H
+    qt = O.Q4_K
+    c, layers, out_norm, w_out, emb = build_model(qt, seed=11, prefill=512, cfg=CFG_HD128)
+    g = to_device(c, layers, out_norm, w_out, True, rope_rows=1024)
+    emb_d = torch.from_numpy(emb).cuda()
+    for step, (pos, tok) in enumerate([(300, 9), (511, 100), (700, 511)]):
+        pos_dev = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        tok_dev = torch.tensor([tok], dtype=torch.int32, device="cuda")
+        x = H.embed(qt, emb_d, c["d_model"], tok_dev)
+        x_ref = O.dequantize(qt, emb[tok:tok + 1], c["d_model"])[0]
+        got = gpu_step(g, x, pos_dev)
+        want = O.decode_step(c, layers, out_norm, w_out, x_ref, pos)
+        err = rel_l2(got, want)
+        assert err <= 1e-5, f"step {step} pos {pos}: rel L2 {err:.3e}"
+        check_caches(c, g, layers, pos)
         for d, w in zip(g["per"], layers):
             for n in ("k_cache", "v_cache"):
                 d[n].copy_(torch.from_numpy(w[n].view(np.int16)))
