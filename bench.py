@@ -339,7 +339,7 @@ def build_decoder(cfg, dev, seed):
 
 
 BATCHED_SHAPES = ((4096, 11008), (11008, 4096))
-BATCHED_B = (1, 4, 8, 16)
+BATCHED_B = (1, 2, 4, 8, 16)
 
 
 def run_batched(dev, stream, reps: int = 20):
@@ -871,7 +871,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                  "replayed between CUDA events",
                        "logits_finite": dec["finite"]},
             "batched": {"workload": "Q4_K [n_out x k] times B activation rows (batched decode), "
-                                    "one launch per 16 rows on the tensor cores (B >= 2)",
+                                    "one launch per 16 rows on the tensor cores (B >= 3; B = 2 as two batch-1 passes)",
                         "us_and_gbs": batched,
                         "timing": "8 rotating weight copies (203 MB > L2) in one CUDA graph, CUDA events, rank 0"},
             "proj70b": {"workload": "70B-shaped Q4_K projections, batch 1: Wq, Wo 8192x8192; Wk, Wv 1024x8192; "
