@@ -188,84 +188,162 @@ def make_inputs(rank: int, dev):
     return mats
 
 
-def cpu_inputs():
-    """Seeded fp32 weights and activations of the sweep's shapes for the CPU
-    legs: the reference's kernel is fp32 (it has no quantized path), so it
-    runs on fp32 rows; its speed does not depend on their values."""
-    rng = np.random.default_rng(2024)
-    return [(name, QT[name], n, k, None, rng.standard_normal(k, dtype=np.float32)) for name, n, k in SWEEP]
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
-# --------------------------------------------------------------------------
-# CPU baseline: the reference's own scalar matmul on dequantized weights
-# --------------------------------------------------------------------------
+def cpu_inputs(rows_cap: int = 1024):
+    """A row sample of each sweep matrix for the CPU legs: the first rows_cap
+    rows of W, fp32 N(0, 0.02) quantized by the oracle's codec (byte-identical
+    to the GPU quantizer), the same rows dequantized to fp32 (the reference
+    stores F32 weights: it has no quantized path), and x ~ N(0, 1)."""
+    from oracle import oracle as O
+    out = []
+    for i, (name, n, k) in enumerate(SWEEP):
+        qt = QT[name]
+        rows = min(rows_cap, n)
+        packed = O.quantize(qt, O.gaussian((rows, k), 0.02, 3000 + i))
+        deq = O.dequantize(qt, packed, k)
+        x = O.gaussian((k,), 1.0, 3100 + i)
+        out.append((name, qt, rows, k, packed, deq, x))
+    return out
 
-def cpu_reference_rate(mats, target_seconds: float = 10.0, max_pass_seconds: float | None = None,
-                       passes: int | None = None):
-    """GB/s of the reference's scalar matmul over the sweep, in the same
-    algorithmic-byte metric. A pass covers the first `rows` rows of each of
-    the eight matrices (all rows unless one pass would exceed
-    max_pass_seconds); passes repeat until target_seconds of CPU time."""
+
+def _timed_passes(one_pass, target_seconds: float, passes: int | None):
+    one_pass()   # warm
+    if passes is None:
+        t0 = time.perf_counter()
+        one_pass()
+        passes = max(1, int(target_seconds / max(time.perf_counter() - t0, 1e-9)))
+    t0 = time.perf_counter()
+    for _ in range(passes):
+        one_pass()
+    return passes, time.perf_counter() - t0
+
+
+def cpu_reference_rate(samples, threads: int, target_seconds: float = 10.0, passes: int | None = None):
+    """GB/s of the reference's scalar matmul (hesa::cpu_matmul_f32, compiled
+    from the reference's sources into oracle/_ref) over the sample's
+    dequantized rows, in the bench's metric (packed bytes of the rows + x + y),
+    rows split over `threads` host threads (1 = as the reference runs it)."""
     import ctypes
     from oracle import oracle as O
     ref = O.ref_lib()
     if ref is None:
         return None
-    threads = O.n_threads_default()
     f32p = ctypes.POINTER(ctypes.c_float)
+    bufs = [(deq, np.ascontiguousarray(x), np.empty(rows, np.float32), rows, k)
+            for _, _, rows, k, _, deq, x in samples]
 
-    rng = np.random.default_rng(7)
-
-    def prep(rows_cap):
-        out = []
-        for name, qt, n, k, _, x in mats:
-            rows = min(rows_cap, n)
-            deq = rng.standard_normal((rows, k), dtype=np.float32) * np.float32(0.02)   # F32 weight rows
-            out.append((qt, rows, k, deq, np.ascontiguousarray(x), np.empty(rows, np.float32)))
-        return out
-
-    def one_pass(samples):
-        for qt, rows, k, deq, x, y in samples:
+    def one_pass():
+        for deq, x, y, rows, k in bufs:
             ref.ref_cpu_matvec_mt(deq.ctypes.data_as(f32p), x.ctypes.data_as(f32p), y.ctypes.data_as(f32p),
                                   rows, k, ctypes.c_float(1.0), threads)
 
-    rows_cap = 1 << 30
-    samples = prep(256)
-    t0 = time.perf_counter()
-    one_pass(samples)
-    t_small = time.perf_counter() - t0
-    full_rows = max(n for _, _, n, _, _, _ in mats)
-    est_full = t_small * full_rows / 256
-    if max_pass_seconds is not None and est_full > max_pass_seconds:
-        rows_cap = max(64, int(256 * max_pass_seconds / max(t_small, 1e-9)))
-    samples = prep(rows_cap)
-    qbytes = sum(rows * row_bytes(qt, k) + 4 * k + 4 * rows for qt, rows, k, _, _, _ in samples)
-    one_pass(samples)  # warm
-    if passes is None:
-        t0 = time.perf_counter()
-        one_pass(samples)
-        t1 = time.perf_counter() - t0
-        passes = max(1, int(target_seconds / max(t1, 1e-9)))
-    t0 = time.perf_counter()
-    for _ in range(passes):
-        one_pass(samples)
-    dt = time.perf_counter() - t0
-    rows_desc = "all rows" if rows_cap >= full_rows else f"the first {rows_cap} rows"
+    qbytes = sum(rows * row_bytes(qt, k) + 4 * k + 4 * rows for _, qt, rows, k, _, _, _ in samples)
+    passes, dt = _timed_passes(one_pass, target_seconds, passes)
+    rows = samples[0][2]
     return {"value": qbytes * passes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
-            "sample": f"hesa::cpu_matmul_f32 (reference scalar kernel on fp32 weight rows; the reference "
-                      f"has no quantized path) over {rows_desc} of each of the 8 sweep matrices, {passes} "
-                      f"pass(es), rows split over {threads} host threads, {dt:.1f} s",
+            "sample": f"hesa::cpu_matmul_f32 (the reference's scalar kernel, compiled from its sources) on the "
+                      f"dequantized fp32 weights of the first {rows} rows of each of the 8 sweep matrices, "
+                      f"{passes} pass(es), rows split over {threads} host thread(s), {dt:.1f} s; credited with "
+                      f"the packed bytes of those rows",
             "seconds": dt, "passes": passes}
+
+
+def cpu_oracle_rate(samples, threads: int, target_seconds: float = 5.0):
+    """GB/s of this build's oracle (fused dequantize + dot in C, OpenMP over
+    rows) on the packed sample rows: plan (ii) of the CPU baseline, labelled
+    as the build's oracle, not the reference."""
+    from oracle import oracle as O
+
+    def one_pass():
+        for _, qt, rows, k, packed, _, x in samples:
+            O.qmatvec(qt, packed, x, n_threads=threads)
+
+    qbytes = sum(rows * row_bytes(qt, k) + 4 * k + 4 * rows for _, qt, rows, k, _, _, _ in samples)
+    passes, dt = _timed_passes(one_pass, target_seconds, None)
+    return {"value": round(qbytes * passes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"oracle_qmatvec (this build's C restatement: fused dequantize + fp32 dot, OpenMP) on the "
+                      f"packed rows of the same sample, {passes} pass(es), {dt:.1f} s"}
+
+
+def cpu_decode_rate(dev, threads: int):
+    """tokens/s of the oracle's decode step at the 7B shape on the host cores:
+    the step is timed with one and with two layers (the same layer twice:
+    its weights quantized on the GPU and copied to the host), and a 32-layer
+    token is extrapolated as t(1) + 31 (t(2) - t(1))."""
+    import torch
+    from oracle import oracle as O
+    cfg = dict(DECODE_7B, n_layer=1)
+    d = build_decoder(cfg, dev, seed=91)
+    L0 = d["layers"][0]
+    host = {n: (L0[n].cpu().numpy().view(np.uint16).copy() if n in ("k_cache", "v_cache")
+                else np.ascontiguousarray(L0[n].cpu().numpy()))
+            for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down", "attn_norm", "ffn_norm", "k_cache",
+                      "v_cache")}
+    w_out = d["w_out"].cpu().numpy()
+    out_norm = d["out_norm"].cpu().numpy()
+    x = O.dequantize(cfg["qtype"], d["emb"][1234:1235].cpu().numpy(), cfg["d_model"])[0]
+    del d
+    torch.cuda.empty_cache()
+    times = {}
+    for nl in (1, 2):
+        c = dict(cfg, n_layer=nl)
+        O.decode_step(c, [host] * nl, out_norm, w_out, x, DECODE_POS, n_threads=threads)   # warm
+        t0 = time.perf_counter()
+        reps = 2
+        for _ in range(reps):
+            O.decode_step(c, [host] * nl, out_norm, w_out, x, DECODE_POS, n_threads=threads)
+        times[nl] = (time.perf_counter() - t0) / reps
+    per_layer = max(times[2] - times[1], 1e-9)
+    token_s = times[1] + (DECODE_7B["n_layer"] - 1) * per_layer
+    return {"tokens_per_s": round(1.0 / token_s, 3), "s_per_token": round(token_s, 3), "cores": threads,
+            "kind": "port",
+            "sample": f"oracle_decode_step at the 7B shape (Q4_K, ctx 2048, pos 2047) timed with 1 and 2 layers "
+                      f"({times[1]:.3f} s, {times[2]:.3f} s), 32 layers extrapolated"}
+
+
+def cpu_baselines(dev):
+    """The CPU legs of the bench line, on the GPU box's host cores (rank 0,
+    N = 1): the reference's own scalar matmul on all host threads (the
+    reported baseline) and on one thread (as the reference runs it), the
+    build's oracle, and the oracle's 7B decode step."""
+    from oracle import oracle as O
+    threads = O.n_threads_default()
+    samples = cpu_inputs()
+    base = cpu_reference_rate(samples, threads, target_seconds=8.0)
+    if base is None:
+        return None
+    out = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    out["value"] = round(out["value"], 3)
+    one = cpu_reference_rate(samples, 1, target_seconds=6.0)
+    out["single_thread"] = {"value": round(one["value"], 3), "unit": "GB/s", "cores": 1, "kind": "reference",
+                            "sample": one["sample"]}
+    out["oracle"] = cpu_oracle_rate(samples, threads)
+    out["decode_7b"] = cpu_decode_rate(dev, threads)
+    out["cpu_model"] = cpu_model()
+    out["host_threads"] = threads
+    return out
 
 
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return 0
-    mats = cpu_inputs()
-    # one step = one pass of the reference kernel over a row sample sized so
-    # the K timed steps take at most ~2 minutes
-    budget = max(0.05, 120.0 / max(args.steps, 1))
-    base = cpu_reference_rate(mats, max_pass_seconds=budget, passes=args.steps)
+    from oracle import oracle as O
+    threads = O.n_threads_default()
+    samples = cpu_inputs()
+    # one step = one pass of the reference kernel over the row sample on all
+    # host threads (about 0.1 s), so the K timed steps stay within minutes
+    base = cpu_reference_rate(samples, threads, passes=args.steps)
     if base is None:
         emit({"impl": "reference", "unavailable": "reference CPU library (oracle/_ref) not built"})
         return 0
@@ -275,7 +353,7 @@ def run_reference(args, rank: int, world: int):
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
            "data": "synthetic (seeded N(0,0.02) weights quantized to GGUF blocks, N(0,1) activations)",
            "config": {"workload": "per-type matvec sweep Q8_0/Q4_K/Q5_K/Q6_K x {4096x11008, 11008x4096} "
-                                  "([n_out x k]), batch 1"},
+                                  "([n_out x k]), batch 1", "cpu_model": cpu_model()},
            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
            "e2e": {"value": round(base["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -705,8 +783,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         # its weights from HBM rather than L2
         per_type = {}
         if rank == 0:
-            for tname in ("Q8_0", "Q4_K", "Q5_K", "Q6_K"):
-                sel = [m for m in dmats if m[0] == tname]
+            # the Q4_0 4096 x 4096 matvec (batch 1) is measured here only: it
+            # is not part of the sweep step
+            g40 = torch.Generator(device=dev)
+            g40.manual_seed(4040)
+            w40 = H.quantize(QT["Q4_0"], torch.randn((4096, 4096), generator=g40, device=dev).mul_(0.02))
+            x40 = torch.randn(4096, generator=g40, device=dev)
+            q40 = [("Q4_0", QT["Q4_0"], 4096, 4096, w40, x40, torch.empty(4096, device=dev),
+                    H.make_workspace(QT["Q4_0"], 4096, 4096, device=dev))]
+            for tname in ("Q4_0", "Q8_0", "Q4_K", "Q5_K", "Q6_K"):
+                sel = [m for m in dmats + q40 if m[0] == tname]
                 pair = sum(m[4].numel() for m in sel)
                 copies = max(2, -(-300_000_000 // pair))
                 rot = [(qt, n, k, wt.clone(), xt, yt, ws) for _ in range(copies)
@@ -822,12 +908,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         achieved = step_bytes() * args.steps / (kernel_ms * 1e-3) / 1e9
         peak, peak_kind = measured_peaks()
         traffic = committed_traffic()
-        cpu_base = None
-        if world == 1:
-            cpu_base = cpu_reference_rate(cpu_inputs(), target_seconds=10.0, max_pass_seconds=2.0)
-            if cpu_base:
-                cpu_base = {k: cpu_base[k] for k in ("value", "unit", "cores", "kind", "sample")}
-                cpu_base["value"] = round(cpu_base["value"], 3)
+        cpu_base = cpu_baselines(dev) if world == 1 else None
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt_ms / args.steps, 4), "higher_is_better": True,

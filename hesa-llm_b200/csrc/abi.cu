@@ -201,6 +201,12 @@ int hesa_cuda_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t
     return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "peer barrier kernel");
 }
 
+int hesa_cuda_set_peer_wait_limit_us(uint32_t limit_us) {
+    if (limit_us > 60u * 1000u * 1000u) return fail(HESA_CUDA_INVALID_ARGUMENT, "peer wait limit above 60 s");
+    hesa_cuda::set_peer_wait_limit(static_cast<unsigned long long>(limit_us) * 1000ull);
+    return HESA_CUDA_OK;
+}
+
 int hesa_cuda_device_status(void* stream, int* status_out) {
     if (!status_out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null status pointer");
     cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
@@ -351,11 +357,8 @@ extern "C" int hesa_cuda_qmatvec_noalloc(int qtype, const void* w, int64_t n_out
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w || !x || !y) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n_out <= 0 || k <= 0 || batch <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "non-positive dimension");
-    if (n_out > hesa_cuda::qmv_noalloc_max_rows())
-        return fail(HESA_CUDA_SHAPE_MISMATCH,
-                    "n_out exceeds the 65536 rows the library's fixed scratch array covers; "
-                    "use hesa_cuda_qmatvec with a caller workspace");
-    if (k >= (int64_t(1) << 31)) return fail(HESA_CUDA_SHAPE_MISMATCH, "dimension too large");
+    if (n_out >= (int64_t(1) << 31) || k >= (int64_t(1) << 31))
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "dimension too large");
     if (k % hesa_cuda::block_elems(qtype) != 0)
         return fail(HESA_CUDA_SHAPE_MISMATCH, "k is not a multiple of the block size");
     if (ldx < k || (batch > 1 && ldy < n_out)) return fail(HESA_CUDA_SHAPE_MISMATCH, "leading dimension too small");
@@ -363,8 +366,27 @@ extern "C" int hesa_cuda_qmatvec_noalloc(int qtype, const void* w, int64_t n_out
     if (!aligned16(x) || !aligned16(y) || (ldx & 3) || (batch > 1 && (ldy & 3)))
         return fail(HESA_CUDA_INVALID_ARGUMENT, "x / y must be 16-byte aligned with ldx, ldy multiples of 4");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e;
-    if (hesa_cuda::qmv_stream_eligible(qtype, w, n_out, k)) {
+    const bool strip = hesa_cuda::qmv_strip_eligible(qtype, w, n_out, k);
+    const bool streaming = !strip && hesa_cuda::qmv_stream_eligible(qtype, w, n_out, k);
+    if (streaming && n_out > hesa_cuda::qmv_noalloc_max_rows())
+        return fail(HESA_CUDA_SHAPE_MISMATCH,
+                    "n_out exceeds the 65536 rows the library's fixed scratch array covers at this k; "
+                    "use hesa_cuda_qmatvec with a caller workspace");
+    // the fixed array's device address, looked up on the first call on this
+    // device whichever kernel the shape takes (so that call, made before any
+    // stream capture, is the only one that queries the runtime for it)
+    uint8_t* scratch = nullptr;
+    cudaError_t e = hesa_cuda::qmv_noalloc_scratch(&scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "no-alloc scratch lookup");
+    if (strip) {
+        // the row-strip kernel reduces inside each CTA: no scratch, any n_out
+        for (int64_t b = 0; b < batch; ++b) {
+            e = hesa_cuda::qmv_strip(qtype, w, n_out, k, x + b * ldx, y + b * ldy, scale, s);
+            if (e != cudaSuccess) return cuda_fail(e, "qmatvec strip kernel");
+        }
+    } else if (streaming) {
+        // rows too long for the strip kernel: the streaming kernel, with its
+        // scratch in the library's fixed array
         for (int64_t b = 0; b < batch; ++b) {
             e = hesa_cuda::qmv_stream_noalloc(qtype, w, n_out, k, x + b * ldx, y + b * ldy, scale, s);
             if (e != cudaSuccess) return cuda_fail(e, "qmatvec no-alloc stream kernel");

@@ -18,8 +18,13 @@ namespace {
 struct PeerFlags {
     uint32_t* flags[kMaxPeers];   // flags[p]: rank p's flag array, mapped here
     uint32_t* epoch;              // this rank's barrier count
+    unsigned long long limit_ns;  // how long to wait for the peers
     int rank, world;
 };
+
+// How long a barrier waits for its peers (set_peer_wait_limit); read when a
+// barrier is enqueued, so a captured graph keeps the value of its capture.
+unsigned long long g_peer_limit_ns = HESA_WAIT_LIMIT_NS;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -49,7 +54,7 @@ __global__ void __launch_bounds__(32) peer_barrier_kernel(PeerFlags f, int* __re
             for (;;) {
                 __nanosleep(100);
                 if (reached(mine, e)) break;
-                if (global_timer_ns() - t0 > HESA_WAIT_LIMIT_NS) {
+                if (global_timer_ns() - t0 > f.limit_ns) {
                     record_status(status, kStatusPeerTimeout);
                     break;
                 }
@@ -71,6 +76,7 @@ cudaError_t peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* 
         f.flags[p] = flags[p];
     }
     f.epoch = epoch;
+    f.limit_ns = g_peer_limit_ns;
     f.rank = rank;
     f.world = world;
     int* status = nullptr;
@@ -79,5 +85,9 @@ cudaError_t peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* 
     peer_barrier_kernel<<<1, 32, 0, stream>>>(f, status);
     return cudaGetLastError();
 }
+
+void set_peer_wait_limit(unsigned long long ns) { g_peer_limit_ns = ns ? ns : HESA_WAIT_LIMIT_NS; }
+
+unsigned long long peer_wait_limit() { return g_peer_limit_ns; }
 
 }  // namespace hesa_cuda

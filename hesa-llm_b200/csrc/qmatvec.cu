@@ -1278,9 +1278,7 @@ static uint8_t* g_noalloc_ptr[64] = {nullptr};
 
 int64_t qmv_noalloc_max_rows() { return static_cast<int64_t>(kNoAllocGroups) * 2; }
 
-cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
-                               float scale, cudaStream_t stream) {
-    if (!qtype_supported(qtype) || n_out > qmv_noalloc_max_rows()) return cudaErrorInvalidValue;
+cudaError_t qmv_noalloc_scratch(uint8_t** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -1291,7 +1289,16 @@ cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t 
         if (e != cudaSuccess) return e;
         g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
     }
-    uint8_t* scratch = g_noalloc_ptr[dev];
+    *out = g_noalloc_ptr[dev];
+    return cudaSuccess;
+}
+
+cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
+                               float scale, cudaStream_t stream) {
+    if (!qtype_supported(qtype) || n_out > qmv_noalloc_max_rows()) return cudaErrorInvalidValue;
+    uint8_t* scratch = nullptr;
+    cudaError_t e = qmv_noalloc_scratch(&scratch);
+    if (e != cudaSuccess) return e;
     // the counters must start at zero; the array keeps whatever the last call
     // (possibly a failed one) left there
     const int R = rows_of(qtype);

@@ -23,6 +23,9 @@ cudaError_t qmv_stream(int qtype, const void* w, int64_t n_out, int64_t k, const
 // Same kernel with its scratch in a fixed device array owned by the library
 // (no caller workspace, no allocation). Rows limited to qmv_noalloc_max_rows().
 int64_t qmv_noalloc_max_rows();
+// Device address of that array on the current device (cudaGetSymbolAddress,
+// looked up once per device).
+cudaError_t qmv_noalloc_scratch(uint8_t** out);
 cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y,
                                float scale, cudaStream_t stream);
 
@@ -62,6 +65,10 @@ cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k
 // bounded: on timeout the status word records kStatusPeerTimeout), then
 // stores it into *epoch. flags[p] is rank p's flag array as mapped here.
 cudaError_t peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch, cudaStream_t stream);
+// How long every peer wait enqueued from now on lasts before it records
+// kStatusPeerTimeout (0 restores the default, 2 s).
+void set_peer_wait_limit(unsigned long long ns);
+unsigned long long peer_wait_limit();
 
 // One warp per row, any k that is a multiple of the block size.
 cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,

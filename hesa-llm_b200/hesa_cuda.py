@@ -75,6 +75,7 @@ SIGNATURES = [
     ("hesa_cuda_peer_close", _int, [_vp]),
     ("hesa_cuda_qmatvec_gather", _int, [_int, _vp, _i64, _i64, _vp, _f, ctypes.POINTER(_vp), _int, _vp, _vp]),
     ("hesa_cuda_peer_barrier", _int, [ctypes.POINTER(_vp), _int, _int, _vp, _vp]),
+    ("hesa_cuda_set_peer_wait_limit_us", _int, [ctypes.c_uint32]),
 ]
 
 
@@ -224,6 +225,12 @@ def qmatvec_gather(qtype: int, w, x, y_peers, world: int, epoch: int, scale: flo
 def peer_barrier(flags, rank: int, world: int, epoch: int, stream=None) -> None:
     arr = (ctypes.c_void_p * world)(*flags)
     _check(lib().hesa_cuda_peer_barrier(arr, rank, world, epoch, _stream_handle(stream)))
+
+
+def set_peer_wait_limit(seconds: float) -> None:
+    """How long each peer barrier waits for the other ranks before it gives up
+    and records device status 4 (0 restores the default, 2 s)."""
+    _check(lib().hesa_cuda_set_peer_wait_limit_us(int(round(seconds * 1e6))))
 
 
 def device_view(ptr: int, numel: int, device=None, dtype: str = "<f4"):

@@ -18,6 +18,11 @@ all-gathered so every rank holds it. Two ways to gather:
 from __future__ import annotations
 
 
+class RankFailure(RuntimeError):
+    """A peer rank did not take part in a step's collective in time (it left,
+    died or hangs): raised instead of waiting for ever."""
+
+
 def row_range(n_out: int, rank: int, world: int) -> tuple[int, int]:
     """Rows [r0, r1) of rank `rank`: floor(rank * n_out / world) .. for rank + 1."""
     if world < 1 or not 0 <= rank < world or n_out < 0:
@@ -74,7 +79,12 @@ class ShardedQMatvec:
         self.local(self.w, x, self.y_slot)
         if scale != 1.0:
             self.y_slot.mul_(scale)
-        dist.all_gather_into_tensor(self.y_all, self.y_slot, group=self.group)
+        try:
+            # the process group's timeout bounds the wait for the other ranks
+            dist.all_gather_into_tensor(self.y_all, self.y_slot, group=self.group)
+        except RuntimeError as e:   # DistBackendError, gloo / NCCL timeouts and closed connections
+            raise RankFailure(f"rank {self.rank}: the all-gather of the sharded matvec did not complete "
+                              f"(a peer rank left or timed out): {e}") from e
         return self.y_all if self.index is None else self.y_all.index_select(0, self.index)
 
 

@@ -101,12 +101,17 @@ HESA_CUDA_API int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int
  * allocate device memory: code embedded in a host program that owns every
  * device allocation through its own pool or budget (a stray cudaMalloc would
  * break that accounting), or a serving loop that must not allocate after
- * start-up. Same arguments, semantics and results as hesa_cuda_qmatvec; it
- * has no counterpart in the reference.
- *   - The kernel's scratch (arrival counters and cross-warp partial sums) is
- *     a fixed 512 KB array inside this library, held on every GPU that loads
- *     it until the process exits. n_out is limited to 65536 rows; larger
- *     n_out is rejected with HESA_CUDA_SHAPE_MISMATCH and a message.
+ * start-up. Same arguments, semantics and results as hesa_cuda_qmatvec
+ * (batch >= 2 takes one batch-1 pass per activation row instead of the
+ * tensor-core path, which needs a workspace); it has no counterpart in the
+ * reference.
+ *   - Shapes the row-strip kernel takes (k <= 24576, the batch-1 path of
+ *     hesa_cuda_qmatvec) need no scratch at all, at any n_out. Longer rows
+ *     run the streaming kernel, whose scratch (arrival counters and
+ *     cross-warp partial sums) is a fixed 512 KB array inside this library,
+ *     held on every GPU that loads it until the process exits; there n_out is
+ *     limited to 65536 rows, and larger n_out is rejected with
+ *     HESA_CUDA_SHAPE_MISMATCH and a message before anything is launched.
  *   - Nothing is allocated: no cudaMalloc, cudaFree or allocating library
  *     call. The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
@@ -315,6 +320,15 @@ HESA_CUDA_API int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_r
  * reach it within that time of one another. */
 HESA_CUDA_API int hesa_cuda_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch,
                                          void* stream);
+
+/* How long each wait for a peer rank lasts (hesa_cuda_peer_barrier) before it
+ * gives up, records device status 4 and returns, in microseconds; 0 restores
+ * the default of 2 s, values above 60 s are refused. Applies to barriers
+ * enqueued after the call (a CUDA graph keeps the limit it was captured
+ * with). The host-side counterpart of a collective timeout: a rank that
+ * dies between steps costs its peers at most this long per barrier, and the
+ * status word tells them why. No counterpart in the reference (one device). */
+HESA_CUDA_API int hesa_cuda_set_peer_wait_limit_us(uint32_t limit_us);
 HESA_CUDA_API int hesa_cuda_clear_device_status(void* stream);
 
 /* Last error message recorded on this host thread ("" if none). */

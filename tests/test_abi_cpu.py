@@ -147,3 +147,10 @@ def test_peer_barrier_and_alloc_reject_bad_arguments():
     assert L.hesa_cuda_peer_open(None, ctypes.byref(ptr)) == 2
     assert L.hesa_cuda_peer_close(None) == 2
     assert L.hesa_cuda_peer_free(None) == 2
+
+
+def test_peer_wait_limit_setting_is_host_side_and_bounded():
+    L = H.lib()
+    assert L.hesa_cuda_set_peer_wait_limit_us(61 * 1000 * 1000) == 2   # above a minute
+    assert L.hesa_cuda_set_peer_wait_limit_us(50 * 1000) == 0
+    assert L.hesa_cuda_set_peer_wait_limit_us(0) == 0                  # back to the 2 s default

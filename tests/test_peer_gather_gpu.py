@@ -7,7 +7,8 @@ the oracle within rel-L2 1e-5; consecutive steps alternate the two output
 parities; several matvecs share one buffer at row offsets; the step replays
 from a CUDA graph with the parity following the device-side barrier count.
 Two GPUs (skipped with fewer): two processes, each holding half of W's rows,
-both end every step with the full y of the oracle."""
+both end every step with the full y of the oracle. A barrier whose peer never
+arrives gives up after the configured wait and reports device status 4."""
 import os
 import socket
 import tempfile
@@ -105,6 +106,44 @@ def test_world1_shared_buffer_and_graph_replay(torch_cuda):
     del graph
     assert H.device_status() == 0
     peers.close()
+
+
+def test_barrier_wait_runs_out_and_reports_status_4(torch_cuda):
+    """A barrier whose peer never arrives (world 2, the peer's flag array a
+    local buffer nobody writes) gives up after the wait limit, records device
+    status 4 and returns; the context stays usable and the next barrier works."""
+    import time
+    import hesa_cuda as H
+    torch = torch_cuda
+    own = torch.zeros(2, dtype=torch.int32, device="cuda")
+    fake_peer = torch.zeros(2, dtype=torch.int32, device="cuda")
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    H.clear_device_status()
+    H.set_peer_wait_limit(0.05)
+    try:
+        t0 = time.time()
+        H.peer_barrier([own.data_ptr(), fake_peer.data_ptr()], 0, 2, epoch.data_ptr())
+        status = H.device_status()
+        elapsed = time.time() - t0
+        assert status == 4, status
+        assert elapsed < 1.5, f"the wait took {elapsed:.2f} s, not the 0.05 s limit"
+        # this rank published its arrival into its slot of the peer's array and
+        # counted the step as ended
+        assert fake_peer.cpu().tolist() == [1, 0]
+        assert int(epoch.item()) == 1
+    finally:
+        H.set_peer_wait_limit(0)
+        H.clear_device_status()
+    assert H.device_status() == 0
+    H.peer_barrier([own.data_ptr()], 0, 1, epoch.data_ptr())     # world 1: completes at once
+    assert H.device_status() == 0 and int(epoch.item()) == 2
+
+
+def test_peer_wait_limit_rejects_values_above_a_minute(torch_cuda):
+    import hesa_cuda as H
+    with pytest.raises(H.HesaError) as ei:
+        H.set_peer_wait_limit(61.0)
+    assert ei.value.code == 2
 
 
 def _free_port():

@@ -52,8 +52,6 @@ def check_rows(y, ref):
 @pytest.mark.parametrize("n_out,k", [(4096, 11008), (11008, 4096)])
 @pytest.mark.parametrize("batch", [2, 4, 8, 16])
 def test_batched_decode_shapes(torch_cuda, name, n_out, k, batch):
-    if name == "Q5_K" and batch in (2, 4):
-        pytest.skip("Q5_K covered at 8 and 16")
     qt = O.QTYPES[name]
     blocks = seeded(qt, n_out, k, 500 + qt + n_out)
     x = O.gaussian((batch, k), 1.0, 600 + batch + k)
@@ -67,6 +65,9 @@ def test_batched_decode_shapes(torch_cuda, name, n_out, k, batch):
     ("Q4_K", 4100, 512, 9),      # ragged last tile, 9 rows: second n-tile per plane
     ("Q5_K", 36, 768, 16),
     ("Q4_K", 64, 32768, 5),      # 128 K slices of one unit
+    ("Q4_K", 64, 32768, 2),      # two rows on the tensor cores (rows too long for the strip kernel)
+    ("Q5_K", 132, 28672, 2),
+    ("Q4_K", 260, 1024, 18),     # 16 + 2 rows: the second launch has two rows
     ("Q4_K", 300, 1024, 20),     # two launch pairs (16 + 4 rows)
     ("Q5_K", 516, 2048, 33),     # three launch pairs
 ])
