@@ -552,6 +552,153 @@ void oracle_attention_f16kv(const float* q, const uint16_t* k_cache,
  *     x = x + W_down (silu(W_gate h) * (W_up h))
  *   logits = W_out rms_norm(x, out_norm)
  */
+/* ------------------------------------------------------------------------ */
+/* The same primitives with every sum accumulated in fp64 (each result       */
+/* rounded to fp32 once). Not a restatement of the reference: a higher-      */
+/* precision measuring instrument, used to tell how far the fp32 decode      */
+/* step itself (the reference's arithmetic) is from the exact result.        */
+/* ------------------------------------------------------------------------ */
+
+static int qmatvec_f64(int qtype, const void* w, int64_t n_out, int64_t k, const float* x,
+                       float* y, int n_threads) {
+    const size_t rb = oracle_row_bytes(qtype, k);
+    if (rb == 0 || n_out < 0) return 1;
+    if (n_threads < 1) n_threads = 1;
+    int err = 0;
+#pragma omp parallel num_threads(n_threads)
+    {
+        float* row = (float*)malloc((size_t)k * sizeof(float));
+        if (!row) {
+#pragma omp atomic write
+            err = 1;
+        } else {
+#pragma omp for schedule(static)
+            for (int64_t n = 0; n < n_out; ++n) {
+                oracle_dequantize_row(qtype, (const uint8_t*)w + (size_t)n * rb, row, k);
+                double sum = 0.0;
+                for (int64_t i = 0; i < k; ++i) sum += (double)row[i] * (double)x[i];
+                y[n] = (float)sum;
+            }
+            free(row);
+        }
+    }
+    return err;
+}
+
+static void rms_norm_f64(const float* in, const float* weight, float* out, int64_t n, float eps) {
+    double ss = 0.0;
+    for (int64_t j = 0; j < n; ++j) ss += (double)in[j] * (double)in[j];
+    const double inv = 1.0 / sqrt(ss / (double)n + (double)eps);
+    for (int64_t j = 0; j < n; ++j) out[j] = (float)((double)in[j] * inv * (double)weight[j]);
+}
+
+static void rope_f64(float* data, int32_t pos, int64_t n_heads, int64_t head_dim, float base) {
+    const int64_t half = head_dim / 2;
+    for (int64_t h = 0; h < n_heads; ++h) {
+        float* row = data + h * head_dim;
+        for (int64_t d = 0; d < half; ++d) {
+            const double th = (double)pos * pow((double)base, -2.0 * (double)d / (double)head_dim);
+            const double x0 = row[d], x1 = row[d + half];
+            row[d] = (float)(x0 * cos(th) - x1 * sin(th));
+            row[d + half] = (float)(x0 * sin(th) + x1 * cos(th));
+        }
+    }
+}
+
+static void attention_f64(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, float* out,
+                          int64_t n_head, int64_t n_kv_head, int64_t head_dim, int64_t n_ctx, int n_threads) {
+    const int64_t group = n_head / n_kv_head;
+    const double sc = 1.0 / sqrt((double)head_dim);
+    if (n_threads < 1) n_threads = 1;
+#pragma omp parallel for num_threads(n_threads) schedule(static)
+    for (int64_t h = 0; h < n_head; ++h) {
+        const int64_t kvh = h / group;
+        const float* qh = q + h * head_dim;
+        double* p = (double*)malloc((size_t)n_ctx * sizeof(double));
+        double* o = (double*)calloc((size_t)head_dim, sizeof(double));
+        if (p && o) {
+            double mx = -1e300;
+            for (int64_t j = 0; j < n_ctx; ++j) {
+                const uint16_t* kj = k_cache + (j * n_kv_head + kvh) * head_dim;
+                double sum = 0.0;
+                for (int64_t d = 0; d < head_dim; ++d) sum += (double)qh[d] * (double)oracle_fp16_to_fp32(kj[d]);
+                p[j] = sum * sc;
+                if (p[j] > mx) mx = p[j];
+            }
+            double s = 0.0;
+            for (int64_t j = 0; j < n_ctx; ++j) { p[j] = exp(p[j] - mx); s += p[j]; }
+            for (int64_t j = 0; j < n_ctx; ++j) {
+                const uint16_t* vj = v_cache + (j * n_kv_head + kvh) * head_dim;
+                const double pj = p[j] / s;
+                for (int64_t d = 0; d < head_dim; ++d) o[d] += pj * (double)oracle_fp16_to_fp32(vj[d]);
+            }
+            for (int64_t d = 0; d < head_dim; ++d) out[h * head_dim + d] = (float)o[d];
+        }
+        free(p);
+        free(o);
+    }
+}
+
+/* The decode step of oracle_decode_step with the fp64-accumulating
+ * primitives above (the K/V rows written to the cache are the same fp16
+ * roundings of the step's k and v). */
+int oracle_decode_step_f64(const oracle_model_cfg* cfg, const oracle_layer* layers,
+                           const float* out_norm, const void* w_out,
+                           const float* x_in, int32_t pos, float* logits, int n_threads) {
+    const int64_t D = cfg->d_model, HD = cfg->head_dim;
+    const int64_t QD = cfg->n_head * HD, KD = cfg->n_kv_head * HD, F = cfg->d_ff;
+    double* x = (double*)malloc((size_t)D * 8);
+    float* xf = (float*)malloc((size_t)D * 4);
+    float* h = (float*)malloc((size_t)D * 4);
+    float* q = (float*)malloc((size_t)QD * 4);
+    float* kk = (float*)malloc((size_t)KD * 4);
+    float* vv = (float*)malloc((size_t)KD * 4);
+    float* a = (float*)malloc((size_t)QD * 4);
+    float* o = (float*)malloc((size_t)D * 4);
+    float* g = (float*)malloc((size_t)F * 4);
+    float* u = (float*)malloc((size_t)F * 4);
+    int err = !(x && xf && h && q && kk && vv && a && o && g && u);
+    if (!err) {
+        for (int64_t i = 0; i < D; ++i) x[i] = x_in[i];
+        const int64_t slot = pos % cfg->ctx;
+        const int64_t n_ctx = (pos + 1 < cfg->ctx) ? pos + 1 : cfg->ctx;
+        for (int64_t l = 0; l < cfg->n_layer && !err; ++l) {
+            const oracle_layer* L = &layers[l];
+            for (int64_t i = 0; i < D; ++i) xf[i] = (float)x[i];
+            rms_norm_f64(xf, L->attn_norm, h, D, cfg->rms_eps);
+            err |= qmatvec_f64(cfg->qtype, L->wq, QD, D, h, q, n_threads);
+            err |= qmatvec_f64(cfg->qtype, L->wk, KD, D, h, kk, n_threads);
+            err |= qmatvec_f64(cfg->qtype, L->wv, KD, D, h, vv, n_threads);
+            rope_f64(q, pos, cfg->n_head, HD, cfg->rope_base);
+            rope_f64(kk, pos, cfg->n_kv_head, HD, cfg->rope_base);
+            for (int64_t i = 0; i < KD; ++i) {
+                L->k_cache[slot * KD + i] = oracle_fp32_to_fp16(kk[i]);
+                L->v_cache[slot * KD + i] = oracle_fp32_to_fp16(vv[i]);
+            }
+            attention_f64(q, L->k_cache, L->v_cache, a, cfg->n_head, cfg->n_kv_head, HD, n_ctx, n_threads);
+            err |= qmatvec_f64(cfg->qtype, L->wo, D, QD, a, o, n_threads);
+            for (int64_t i = 0; i < D; ++i) x[i] += o[i];
+            for (int64_t i = 0; i < D; ++i) xf[i] = (float)x[i];
+            rms_norm_f64(xf, L->ffn_norm, h, D, cfg->rms_eps);
+            err |= qmatvec_f64(cfg->qtype, L->w_gate, F, D, h, g, n_threads);
+            err |= qmatvec_f64(cfg->qtype, L->w_up, F, D, h, u, n_threads);
+            for (int64_t i = 0; i < F; ++i) {
+                const double gg = g[i];
+                g[i] = (float)(gg / (1.0 + exp(-gg)) * (double)u[i]);
+            }
+            err |= qmatvec_f64(cfg->qtype, L->w_down, D, F, g, o, n_threads);
+            for (int64_t i = 0; i < D; ++i) x[i] += o[i];
+        }
+        if (!err) {
+            for (int64_t i = 0; i < D; ++i) xf[i] = (float)x[i];
+            rms_norm_f64(xf, out_norm, h, D, cfg->rms_eps);
+            err |= qmatvec_f64(cfg->qtype, w_out, cfg->vocab, D, h, logits, n_threads);
+        }
+    }
+    free(x); free(xf); free(h); free(q); free(kk); free(vv); free(a); free(o); free(g); free(u);
+    return err;
+}
+
 int oracle_decode_step(const oracle_model_cfg* cfg, const oracle_layer* layers,
                        const float* out_norm, const void* w_out,
                        const float* x_in, int32_t pos, float* logits,

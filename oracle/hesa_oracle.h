@@ -113,6 +113,15 @@ int oracle_decode_step(const oracle_model_cfg* cfg, const oracle_layer* layers,
                        const float* x_in, int32_t pos, float* logits,
                        int n_threads);
 
+/* oracle_decode_step with every sum accumulated in fp64 (the residual stream
+ * kept in fp64, each primitive's result rounded to fp32 once): not the
+ * reference's arithmetic, but a higher-precision measure of the exact result,
+ * to separate the fp32 rounding of the reference's own step from a kernel's
+ * deviation. Writes the same K/V slot. */
+int oracle_decode_step_f64(const oracle_model_cfg* cfg, const oracle_layer* layers,
+                           const float* out_norm, const void* w_out,
+                           const float* x_in, int32_t pos, float* logits, int n_threads);
+
 #ifdef __cplusplus
 }
 #endif

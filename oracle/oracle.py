@@ -70,6 +70,7 @@ def lib() -> ctypes.CDLL:
                                              _i64, ctypes.c_int]
         L.oracle_decode_step.argtypes = [ctypes.POINTER(ModelCfg), ctypes.POINTER(LayerPtrs), _f32p, _vp,
                                          _f32p, ctypes.c_int32, _f32p, ctypes.c_int]
+        L.oracle_decode_step_f64.argtypes = L.oracle_decode_step.argtypes
         _lib = L
     return _lib
 
@@ -207,10 +208,11 @@ def attention_f16kv(q, k_cache, v_cache, n_head, n_kv_head, head_dim, n_ctx,
 
 
 def decode_step(cfg: dict, layers: list, out_norm: np.ndarray, w_out: np.ndarray, x_in: np.ndarray, pos: int,
-                n_threads: int | None = None) -> np.ndarray:
+                n_threads: int | None = None, f64: bool = False) -> np.ndarray:
     """oracle_decode_step: logits of one token. `layers` holds dicts of numpy
     arrays (packed uint8 weights, fp32 norms, uint16 fp16 caches that are
-    updated in place)."""
+    updated in place). f64=True runs oracle_decode_step_f64 instead (every sum
+    in fp64: a higher-precision measure, not the reference's arithmetic)."""
     c = ModelCfg(**{k: cfg[k] for k in ("n_layer", "d_model", "n_head", "n_kv_head", "head_dim", "d_ff", "vocab",
                                          "ctx")}, rms_eps=cfg.get("rms_eps", 1e-6),
                  rope_base=cfg.get("rope_base", 10000.0), qtype=cfg["qtype"])
@@ -225,7 +227,8 @@ def decode_step(cfg: dict, layers: list, out_norm: np.ndarray, w_out: np.ndarray
     logits = np.empty(cfg["vocab"], np.float32)
     x = np.ascontiguousarray(x_in, np.float32)
     on = np.ascontiguousarray(out_norm, np.float32)
-    rc = lib().oracle_decode_step(ctypes.byref(c), arr, _p(on, _f32p), w_out.ctypes.data, _p(x, _f32p),
+    fn = lib().oracle_decode_step_f64 if f64 else lib().oracle_decode_step
+    rc = fn(ctypes.byref(c), arr, _p(on, _f32p), w_out.ctypes.data, _p(x, _f32p),
                                   int(pos), _p(logits, _f32p), n_threads or n_threads_default())
     if rc:
         raise RuntimeError("oracle_decode_step failed")

@@ -11,8 +11,13 @@ the 32000-row LM head. The weights come from the GPU quantizer, which is
 byte-identical to the oracle's (tests/test_quantize_gpu.py), and are copied
 to the host for the oracle, so set-up takes seconds.
 
-Bars: logits within rel-L2 1e-5; the KV slot the step writes within one fp16
-rounding of the oracle's and every other slot untouched."""
+Bars: logits within rel-L2 1e-5 of the oracle at 2 layers. At 32 layers the
+oracle's own fp32 rounding (the reference's arithmetic: sequential fp32 sums)
+is ~1.6e-5 from the exact logits, measured with the oracle's fp64-accumulating
+decode step; there the kernels must be within 1e-5 of that exact result and no
+further from it than the oracle (measured on B200: 9.1e-6 against the
+oracle's 1.59e-5). The KV slot the step writes within one fp16 rounding of the
+oracle's and every other slot untouched."""
 import numpy as np
 import pytest
 
@@ -111,8 +116,22 @@ def test_decode_step_7b_widths_match_oracle(n_layer):
 
     x_ref = O.dequantize(qt, emb[tok:tok + 1].cpu().numpy(), cfg["d_model"])[0]
     assert np.array_equal(x.cpu().numpy(), x_ref)            # exact embedding row
-    want = O.decode_step(cfg, host_layers, out_norm.cpu().numpy(), w_out.cpu().numpy(), x_ref, POS)
-    err = rel_l2(got, want)
-    assert err <= 1e-5, f"{n_layer} layers: logits rel L2 {err:.3e}"
+    on, wo = out_norm.cpu().numpy(), w_out.cpu().numpy()
+    # the exact result, measured with every sum in fp64, first (the fp32 run
+    # after it leaves its own K/V rows in the host caches for check_caches)
+    exact = O.decode_step(cfg, host_layers, on, wo, x_ref, POS, f64=True)
+    want = O.decode_step(cfg, host_layers, on, wo, x_ref, POS)
+    err, err_exact, ref_exact = rel_l2(got, want), rel_l2(got, exact), rel_l2(want, exact)
+    if n_layer <= 8:
+        assert err <= 1e-5, f"{n_layer} layers: logits rel L2 {err:.3e} against the oracle"
+    else:
+        # Through 32 layers the fp32 rounding of the reference's own step (a
+        # sequential fp32 sum of 4096 or 11008 terms per output, ~3e-6 each)
+        # compounds to ~1.6e-5 of the exact logits, more than the bar itself.
+        # The bar is then held against the exact result, and the kernels must
+        # be at least as close to it as the reference's arithmetic is.
+        assert err_exact <= 1e-5, f"{n_layer} layers: rel L2 {err_exact:.3e} against the exact logits"
+        assert err_exact <= ref_exact, f"kernels {err_exact:.3e} vs the reference's fp32 {ref_exact:.3e}"
+        assert err <= 3e-5, f"{n_layer} layers: rel L2 {err:.3e} against the oracle"
     check_caches(cfg, dev_layers, host_layers, POS)
     assert H.device_status() == 0
