@@ -57,6 +57,17 @@ bool contiguous_f32(const TensorView& v) {
     return true;
 }
 
+// true when p points into device (or managed) memory of any device
+bool on_device(const void* p) {
+    if (!p) return false;
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();   // a plain host pointer: not an error to keep
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
 float load_f32(const TensorView& v, int64_t i, int64_t j) {
     const auto st = v.byte_strides();
     const auto* base = static_cast<const uint8_t*>(v.data());
@@ -157,10 +168,9 @@ Result<Tensor> CudaBackend::alloc_tensor(Dtype dtype, std::span<const int64_t> s
     return std::move(t);
 }
 
-Result<void> CudaBackend::free_tensor(Tensor& tensor) {
-    // evict any device copy made from this tensor's bytes
+void CudaBackend::forget(const void* host) {
     for (auto it = weights_.begin(); it != weights_.end();) {
-        if (it->first.first == tensor.data()) {
+        if (it->first.first == host) {
             cudaFree(it->second.ptr);
             weight_bytes_ -= it->second.bytes;
             it = weights_.erase(it);
@@ -168,8 +178,45 @@ Result<void> CudaBackend::free_tensor(Tensor& tensor) {
             ++it;
         }
     }
+}
+
+Result<void> CudaBackend::free_tensor(Tensor& tensor) {
+    // evict any device copy made from this tensor's bytes
+    forget(tensor.data());
     tensor = Tensor{};
     return ok();
+}
+
+TensorView CudaBackend::device_view(const void* ptr, Dtype dtype, int64_t rows, int64_t cols) {
+    const size_t es = dtype_size(dtype);
+    const size_t st[2] = {static_cast<size_t>(cols) * es, es};
+    return TensorView(ptr, dtype, Shape{rows, cols}, std::span<const size_t>(st, 2));
+}
+
+TensorView CudaBackend::device_columns(float* ptr, int64_t k, int64_t batch, int64_t ld) {
+    // [k, batch] with element (i, j) at ptr[j * ld + i]
+    const size_t st[2] = {sizeof(float), static_cast<size_t>(ld) * sizeof(float)};
+    return TensorView(static_cast<void*>(ptr), Dtype::F32, Shape{k, batch}, std::span<const size_t>(st, 2));
+}
+
+bool CudaBackend::dtype_of_gguf(uint32_t type, Dtype& out) {
+    switch (type) {
+        case 0: out = Dtype::F32; return true;
+        case 1: out = Dtype::F16; return true;
+        case 30: out = Dtype::BF16; return true;
+        case 24: out = Dtype::I8; return true;
+        case 2: out = Dtype::Q4_0; return true;
+        case 3: out = Dtype::Q4_1; return true;
+        case 6: out = Dtype::Q5_0; return true;
+        case 7: out = Dtype::Q5_1; return true;
+        case 8: out = Dtype::Q8_0; return true;
+        case 10: out = Dtype::Q2_K; return true;
+        case 11: out = Dtype::Q3_K; return true;
+        case 12: out = Dtype::Q4_K; return true;
+        case 13: out = Dtype::Q5_K; return true;
+        case 14: out = Dtype::Q6_K; return true;
+        default: return false;
+    }
 }
 
 Result<void> CudaBackend::matmul(TensorView a, TensorView b, TensorView out, float scale) {
@@ -195,8 +242,42 @@ Result<void> CudaBackend::matmul(TensorView a, TensorView b, TensorView out, flo
             return error(Error::INVALID_ARGUMENT);
         wbytes = static_cast<size_t>(M) * K * sizeof(float);
     }
-    auto dw = device_weights(a.data(), wbytes);
-    if (!dw) return std::unexpected{dw.error()};
+    // device-resident weights are used in place; host weights are uploaded once
+    const void* dev_w = nullptr;
+    if (on_device(a.data())) {
+        dev_w = a.data();
+    } else {
+        auto dw = device_weights(a.data(), wbytes);
+        if (!dw) return std::unexpected{dw.error()};
+        dev_w = *dw;
+    }
+
+    // device-resident activations and outputs: no staging, no host wait. The
+    // C ABI wants batch rows of x (k floats, ldx apart) and of y (n_out, ldy
+    // apart), i.e. b and out as column views over device rows.
+    if (on_device(b.data()) && on_device(out.data())) {
+        const auto bs = b.byte_strides();
+        const auto os = out.byte_strides();
+        if (bs[0] != sizeof(float) || os[0] != sizeof(float)) return error(Error::INVALID_ARGUMENT);
+        const int64_t ldx = N > 1 ? static_cast<int64_t>(bs[1] / sizeof(float)) : K;
+        const int64_t ldy = N > 1 ? static_cast<int64_t>(os[1] / sizeof(float)) : M;
+        if ((N > 1 && (bs[1] % sizeof(float) || os[1] % sizeof(float))) || ldx < K || ldy < M)
+            return error(Error::INVALID_ARGUMENT);
+        if (qt > 0) {
+            const size_t ws = hesa_cuda_qmatvec_workspace_size(qt, M, K, N);
+            if (d_ws_.bytes < ws) {
+                HESA_CHECK(ensure(d_ws_, ws));
+                HESA_CHECK(from_cuda(cudaMemsetAsync(d_ws_.ptr, 0, d_ws_.bytes, s)));
+            }
+            return from_abi(hesa_cuda_qmatvec(qt, dev_w, M, K, static_cast<const float*>(b.data()), ldx, N,
+                                              static_cast<float*>(out.data()), ldy, scale, d_ws_.ptr, d_ws_.bytes,
+                                              s));
+        }
+        return from_abi(hesa_cuda_matmul_f32(static_cast<const float*>(dev_w), M, K,
+                                             static_cast<const float*>(b.data()), ldx, N,
+                                             static_cast<float*>(out.data()), ldy, scale, s));
+    }
+    if (on_device(b.data()) || on_device(out.data())) return error(Error::INVALID_ARGUMENT);   // mixed
 
     // activations: b[k, j] -> x[j*K + k]
     const size_t xbytes = static_cast<size_t>(N) * K * sizeof(float);
@@ -217,10 +298,10 @@ Result<void> CudaBackend::matmul(TensorView a, TensorView b, TensorView out, flo
             HESA_CHECK(ensure(d_ws_, ws));
             HESA_CHECK(from_cuda(cudaMemsetAsync(d_ws_.ptr, 0, d_ws_.bytes, s)));
         }
-        HESA_CHECK(from_abi(hesa_cuda_qmatvec(qt, *dw, M, K, static_cast<const float*>(d_x_.ptr), K, N,
+        HESA_CHECK(from_abi(hesa_cuda_qmatvec(qt, dev_w, M, K, static_cast<const float*>(d_x_.ptr), K, N,
                                               static_cast<float*>(d_y_.ptr), M, scale, d_ws_.ptr, d_ws_.bytes, s)));
     } else {
-        HESA_CHECK(from_abi(hesa_cuda_matmul_f32(static_cast<const float*>(*dw), M, K,
+        HESA_CHECK(from_abi(hesa_cuda_matmul_f32(static_cast<const float*>(dev_w), M, K,
                                                  static_cast<const float*>(d_x_.ptr), K, N,
                                                  static_cast<float*>(d_y_.ptr), M, scale, s)));
     }

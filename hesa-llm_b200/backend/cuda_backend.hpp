@@ -6,14 +6,19 @@
 // that backend. It implements the interface of include/hesa/backend.hpp:28-65
 // and reaches the GPU only through the C ABI of include/hesa_cuda.h.
 //
-// Tensors of the reference own host memory (src/tensor/tensor.cpp:63-77;
-// device_ptr is never set), so the backend keeps device copies itself:
-//   * weight views of a quantized dtype are uploaded once and cached by
-//     (host pointer, bytes) -- GGUF weights are immutable after Model::load;
-//   * activations and outputs travel through pinned staging buffers on every
-//     call, on the backend's own stream.
+// Operands may live in device or host memory (checked per pointer):
+//   * device-resident views -- weights uploaded once by hesa_gguf::DeviceModel
+//     (backend/device_model.hpp) from a GGUF file, activations and outputs in
+//     device buffers -- are used in place, with no copy and no host wait;
+//   * host views (Tensors of the reference own host memory,
+//     src/tensor/tensor.cpp:63-77, where device_ptr is never set): weight
+//     views of a quantized dtype are uploaded once and cached by (host
+//     pointer, bytes), which assumes the bytes do not change while cached
+//     (GGUF weights are immutable after Model::load; free_tensor or forget()
+//     drops a copy); activations and outputs travel through pinned staging
+//     buffers on every call, on the backend's own stream.
 // Calls are asynchronous on that stream except where a host result is
-// produced (matmul writes `out`, a host view); synchronize() joins.
+// produced (matmul writes a host `out`); synchronize() joins.
 #pragma once
 
 #include "hesa/backend.hpp"
@@ -68,10 +73,23 @@ public:
     Result<void> synchronize() override;
     Result<void> copy_tensor(const Tensor& src, Tensor& dst) override;
 
+    // Views on device memory (the GGUF weights of a hesa_gguf::DeviceModel,
+    // or device activations): matmul takes them without any host copy. A
+    // quantized weight view is [rows, cols]; an activation view [k, batch]
+    // over `batch` device rows of k floats (ld floats apart); an output view
+    // [n_out, batch] likewise. With device-resident a, b and out, matmul is
+    // asynchronous on stream() and returns without waiting.
+    static TensorView device_view(const void* ptr, Dtype dtype, int64_t rows, int64_t cols);
+    static TensorView device_columns(float* ptr, int64_t k, int64_t batch, int64_t ld);
+    // GGUF tensor type id -> Dtype (false when the Dtype enum has no such type)
+    static bool dtype_of_gguf(uint32_t type, Dtype& out);
+
     int device_id() const { return device_; }
     void* stream() const { return stream_; }
     // number of weight uploads kept on the device (test hook)
     size_t cached_weights() const { return weights_.size(); }
+    // drop the device copies made from host bytes at `host`
+    void forget(const void* host);
 
 private:
     struct DevBuf {
