@@ -520,9 +520,11 @@ def run_proj70b(dev, stream, rank: int, world: int, reps: int = 20):
     return ms
 
 
-def run_decode(dev, stream, steps: int, warmup: int, pg=None):
+def run_decode(dev, stream, steps: int, warmup: int, pg=None, rank: int = 0, world: int = 1):
     """tokens/s of the 7B-shaped Q4_K decode step (embedding lookup + every
-    layer + LM head), one CUDA graph per token, device-timed."""
+    layer + LM head) of ONE sequence, one CUDA graph per token, device-timed.
+    At N > 1 the sequence is decoded on all N GPUs together: heads, KV caches
+    and row shares of every projection per rank (sharding.ShardedDecoder)."""
     import torch
     import hesa_cuda as H
     cfg = DECODE_7B
@@ -531,11 +533,23 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None):
     logits = torch.empty(cfg["vocab"], dtype=torch.float32, device=dev)
     pos_dev = torch.tensor([DECODE_POS], dtype=torch.int32, device=dev)
     tok_dev = torch.tensor([1234], dtype=torch.int32, device=dev)
+    dec = None
+    if world > 1:
+        import sharding
+        dec = sharding.ShardedDecoder(cfg, d, rank, world, device=dev)
+        logits = dec.logits()
+        del d["layers"], d["arr"]   # the full model's weights: every rank keeps its shards only
+        torch.cuda.empty_cache()
+        torch.cuda.synchronize(dev)
+        pg.barrier()   # the ranks meet their first peer barrier within its wait limit
 
     def step():
         H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok_dev, out=x, stream=stream)
-        H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos_dev, logits, d["ws"],
-                      stream=stream)
+        if dec is not None:
+            dec.step(x, pos_dev, stream=stream)
+        else:
+            H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos_dev, logits, d["ws"],
+                          stream=stream)
 
     with torch.cuda.stream(stream):
         for _ in range(2):
@@ -560,6 +574,11 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None):
         ms = e0.elapsed_time(e1) / steps
     ok = bool(torch.isfinite(logits).all().item()) and H.device_status(stream) == 0
     del graph
+    if dec is not None:
+        torch.cuda.synchronize(dev)
+        pg.barrier()
+        dec.close()
+        pg.barrier()
     return dict(ms=ms, finite=ok, bytes_token=d["bytes_token"], weight_bytes=d["weight_bytes"],
                 kv_bytes=d["kv_bytes"])
 
@@ -891,7 +910,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             gathered_ok = bool(torch.equal(peers.output(par), y_all))
 
     # the 7B-shaped Q4_K decode step, one full replica per rank
-    dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg)
+    dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg, rank=rank, world=world)
     batched = run_batched(dev, stream) if rank == 0 else None
     p70_ms = run_proj70b(dev, stream, rank, world)
 
@@ -943,11 +962,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             "decode": {"model": "Llama-shaped 7B (32 layers, d_model 4096, 32 heads x 128, FFN 11008 SwiGLU, "
                                 "vocab 32000, RMSNorm, RoPE 10000), Q4_K, random init N(0, 0.02)",
                        "ctx": DECODE_7B["ctx"], "pos": DECODE_POS,
-                       "tokens_per_s": round(world * 1000.0 / dec_ms, 1), "ms_per_token": round(dec_ms, 4),
+                       "tokens_per_s": round(1000.0 / dec_ms, 1), "ms_per_token": round(dec_ms, 4),
                        "bytes_per_token": dec["bytes_token"],
                        "gbs": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9, 1),
-                       "frac_of_hbm": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9 / peak, 4),
-                       "parallelism": "one full replica per GPU" if world > 1 else "single GPU",
+                       "frac_of_hbm": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9 / (peak * world), 4),
+                       "parallelism": (f"one sequence on {world} GPUs: heads, KV caches and row shares of every "
+                                       "projection per rank, the four gathers per layer fused into the kernels "
+                                       "(peer stores + a barrier at the end of each grid)" if world > 1
+                                       else "single GPU"),
                        "timing": "embedding lookup + 32 layers + LM head captured as one CUDA graph per token, "
                                  "replayed between CUDA events",
                        "logits_finite": dec["finite"]},

@@ -15,6 +15,7 @@
 // The position is read from device memory so a captured CUDA graph can be
 // replayed for every token.
 #include "hesa_common.cuh"
+#include "peer_sync.cuh"
 #include "decode_ops.h"
 #include "qmatvec.h"
 
@@ -285,6 +286,12 @@ struct AttnRope {
     const float* table;   // rope table [table_rows][head_dim]: cos, then sin
     int table_rows;
     int* status;
+    // head-sharded decode: head h's output goes to peer_out[p] + h * head_dim
+    // on every rank p (this rank's first head's place in rank p's buffer),
+    // then the cross-rank barrier at the end of the grid; peer_world 0: out
+    float* peer_out[kPeerSyncMax];
+    int peer_world;
+    PeerSync sync;
 };
 
 template <int DPL, bool ROPE>  // dims per lane (head_dim / 32)
@@ -567,7 +574,12 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
                 float a = 0.f;
 #pragma unroll
                 for (int w = 0; w < kAttnWarps; ++w) a = fmaf(s_acc[w][lane * DPL + i], f[w], a);
-                out[static_cast<int64_t>(h) * head_dim + lane * DPL + i] = a * inv;
+                const int64_t o = static_cast<int64_t>(h) * head_dim + lane * DPL + i;
+                if (ri.peer_world == 0) {
+                    out[o] = a * inv;
+                } else {
+                    for (int p = 0; p < ri.peer_world; ++p) ri.peer_out[p][o] = a * inv;
+                }
             }
             if (lane == 0) {
                 cuda::atomic_ref<int, cuda::thread_scope_device> cnt(counters[h]);
@@ -575,6 +587,7 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
             }
         }
     }
+    if constexpr (ROPE) grid_end_peer_barrier(ri.sync, ri.status);   // no-op unless head-sharded
 }
 
 int grid_for(int64_t n, int threads, int cap = 148 * 8) {
@@ -744,10 +757,33 @@ cudaError_t attention_rope(const float* q, const float* k_new, const float* v_ne
                            int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
                            int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
                            cudaStream_t s) {
+    return attention_rope_shard(q, k_new, v_new, kc, vc, out, n_head, n_kv_head, head_dim, table, table_rows, ctx,
+                                pos_dev, workspace, nullptr, 0, PeerSync{}, s);
+}
+
+cudaError_t attention_rope_shard(const float* q, const float* k_new, const float* v_new, void* kc, void* vc,
+                                 float* out, int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
+                                 int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
+                                 float* const* peer_out, int peer_world, const PeerSync& sync, cudaStream_t s) {
     int* status = nullptr;
     cudaError_t e = status_word(&status);
     if (e != cudaSuccess) return e;
-    const AttnRope ri = {k_new, v_new, static_cast<__half*>(kc), static_cast<__half*>(vc), table, table_rows, status};
+    if (peer_world < 0 || peer_world > kPeerSyncMax || (peer_world > 0 && (!peer_out || sync.world != peer_world)))
+        return cudaErrorInvalidValue;
+    AttnRope ri = {};
+    ri.k_new = k_new;
+    ri.v_new = v_new;
+    ri.kc = static_cast<__half*>(kc);
+    ri.vc = static_cast<__half*>(vc);
+    ri.table = table;
+    ri.table_rows = table_rows;
+    ri.status = status;
+    ri.peer_world = peer_world;
+    for (int p = 0; p < peer_world; ++p) {
+        if (!peer_out[p]) return cudaErrorInvalidValue;
+        ri.peer_out[p] = peer_out[p];
+    }
+    ri.sync = sync;
     return attention_any<true>(q, kc, vc, out, n_head, n_kv_head, head_dim, ctx, pos_dev, 0, workspace, ri, s);
 }
 

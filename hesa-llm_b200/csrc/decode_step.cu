@@ -24,6 +24,7 @@
 #include "hesa_common.cuh"
 #include "qmatvec.h"
 #include "qtypes.cuh"
+#include "peer_sync.cuh"
 
 #include <cstdint>
 
@@ -255,3 +256,136 @@ int hesa_cuda_decode_step(const hesa_cuda_model* m, const hesa_cuda_layer* layer
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// head-sharded decode step
+// ---------------------------------------------------------------------------
+
+extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hesa_cuda_shard* sh,
+                                             const hesa_cuda_layer* layers, const float* out_norm, const void* w_out,
+                                             const float* rope_table, int32_t rope_rows, const float* x_embed,
+                                             const int32_t* pos_dev, void* workspace, size_t workspace_bytes,
+                                             void* stream) {
+    using namespace hesa_cuda;
+    if (!model_ok(m)) return record_error(HESA_CUDA_SHAPE_MISMATCH, "bad model shape");
+    if (!sh || !layers || !out_norm || !w_out || !rope_table || !x_embed || !pos_dev || !workspace)
+        return record_error(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    const int W = sh->world, r = sh->rank;
+    if (W < 1 || W > kPeerSyncMax || r < 0 || r >= W) return record_error(HESA_CUDA_INVALID_ARGUMENT, "bad rank / world");
+    if (!sh->x_peers || !sh->a_peers || !sh->gu_peers || !sh->logits_peers || !sh->flags || !sh->epoch || !sh->ticket)
+        return record_error(HESA_CUDA_INVALID_ARGUMENT, "null shard buffer array");
+    for (int p = 0; p < W; ++p)
+        if (!sh->x_peers[p] || !sh->a_peers[p] || !sh->gu_peers[p] || !sh->logits_peers[p] || !sh->flags[p])
+            return record_error(HESA_CUDA_INVALID_ARGUMENT, "null peer buffer");
+    if (m->n_head % W != 0 || m->n_kv_head % W != 0)
+        return record_error(HESA_CUDA_SHAPE_MISMATCH, "n_head and n_kv_head must be multiples of world");
+    if (rope_rows <= 0) return record_error(HESA_CUDA_SHAPE_MISMATCH, "empty rope table");
+    const Layout L = layout(m);
+    if (workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return record_error(HESA_CUDA_INVALID_ARGUMENT, "workspace too small or not 256-byte aligned");
+
+    const int qt = m->qtype;
+    const int64_t D = m->d_model, HD = m->head_dim, F = m->d_ff, V = m->vocab;
+    const int64_t QD = static_cast<int64_t>(m->n_head) * HD;
+    const int64_t hl = m->n_head / W, kvl = m->n_kv_head / W;
+    const int64_t qd_r = hl * HD, kd_r = kvl * HD;
+    auto share = [&](int64_t n, int64_t& a, int64_t& b) {
+        a = n * r / W;
+        b = n * (r + 1) / W;
+    };
+    int64_t d0, d1, f0, f1, v0, v1;
+    share(D, d0, d1);
+    share(F, f0, f1);
+    share(V, v0, v1);
+    const size_t rb_d = hesa_cuda_row_bytes(qt, D), rb_qd = hesa_cuda_row_bytes(qt, QD),
+                 rb_f = hesa_cuda_row_bytes(qt, F);
+    if (!rb_d || !rb_qd || !rb_f)
+        return record_error(HESA_CUDA_SHAPE_MISMATCH, "d_model, n_head*head_dim and d_ff must be block multiples");
+    if (d1 <= d0 || f1 <= f0 || v1 <= v0) return record_error(HESA_CUDA_SHAPE_MISMATCH, "an empty row share");
+    using SI = StripInput;
+    if (!qmv_strip_fused_eligible(qt, layers[0].wq, qd_r + 2 * kd_r, D, SI::kRmsNorm) ||
+        !qmv_strip_fused_eligible(qt, layers[0].wo, d1 - d0, QD, SI::kPlain) ||
+        !qmv_strip_fused_eligible(qt, layers[0].w_gate, 2 * (f1 - f0), D, SI::kRmsNorm) ||
+        !qmv_strip_fused_eligible(qt, layers[0].w_down, d1 - d0, F, SI::kSiluMul) ||
+        !qmv_strip_fused_eligible(qt, w_out, v1 - v0, D, SI::kRmsNorm))
+        return record_error(HESA_CUDA_SHAPE_MISMATCH, "a shard does not fit the row-strip kernel");
+    if ((HD != 64 && HD != 128 && HD != 256) || m->ctx > 131072)
+        return record_error(HESA_CUDA_SHAPE_MISMATCH, "head_dim must be 64, 128 or 256, ctx <= 131072");
+
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* q = reinterpret_cast<float*>(ws + L.qkv);
+    float* k = q + qd_r;
+    float* v = k + kd_r;
+    void* att_ws = ws + L.att;
+    float* x_own = sh->x_peers[r];
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    PeerSync ps = {};
+    for (int p = 0; p < W; ++p) ps.flags[p] = sh->flags[p];
+    ps.epoch = sh->epoch;
+    ps.ticket = reinterpret_cast<int*>(sh->ticket);
+    ps.limit_ns = peer_wait_limit();
+    ps.rank = r;
+    ps.world = W;
+    // every gathered vector: this rank's part lands at `off` of every rank's buffer
+    auto peers = [&](float* const* bufs, int64_t off, int64_t n_rows, float* const* bufs2, int64_t off2,
+                     int64_t split) {
+        PeerOut o = {};
+        for (int p = 0; p < W; ++p) {
+            o.y[0][p] = o.y[1][p] = bufs[p] + off;
+            o.y2[0][p] = o.y2[1][p] = bufs2 ? bufs2[p] + off2 : nullptr;
+        }
+        o.split = static_cast<int>(bufs2 ? split : n_rows);
+        o.epoch = sh->epoch;
+        o.world = W;
+        return o;
+    };
+    auto strip = [&](const void* w, int64_t n, int64_t kk, const float* xin, SI in, const float* nw,
+                     const float* resid, const PeerOut& o) {
+        const cudaError_t e = qmv_strip_shard(qt, w, n, kk, xin, in, nw, m->rms_eps, resid, 1.0f, o, ps, s);
+        return e == cudaSuccess ? HESA_CUDA_OK : record_cuda_error(e, "sharded matvec");
+    };
+
+    int rc = HESA_CUDA_OK;
+    if (x_embed != x_own) {
+        const cudaError_t ce = cudaMemcpyAsync(x_own, x_embed, D * 4, cudaMemcpyDeviceToDevice, s);
+        if (ce != cudaSuccess) rc = record_cuda_error(ce, "copy of the embedding");
+    }
+    float* a_out[kPeerSyncMax] = {};
+    for (int p = 0; p < W; ++p) a_out[p] = sh->a_peers[p] + r * qd_r;
+    for (int l = 0; l < m->n_layer && rc == HESA_CUDA_OK; ++l) {
+        const hesa_cuda_layer& Ly = layers[l];
+        if (!Ly.wq || !Ly.wk || !Ly.wv || !Ly.wo || !Ly.w_gate || !Ly.w_up || !Ly.w_down || !Ly.attn_norm ||
+            !Ly.ffn_norm || !Ly.k_cache || !Ly.v_cache)
+            return record_error(HESA_CUDA_INVALID_ARGUMENT, "null pointer in a layer");
+        const uint8_t* wq = static_cast<const uint8_t*>(Ly.wq);
+        if (Ly.wk != wq + qd_r * rb_d || Ly.wv != wq + (qd_r + kd_r) * rb_d ||
+            Ly.w_up != static_cast<const uint8_t*>(Ly.w_gate) + (f1 - f0) * rb_d)
+            return record_error(HESA_CUDA_INVALID_ARGUMENT, "Q|K|V and gate|up shards must be joined");
+        if ((reinterpret_cast<uintptr_t>(Ly.k_cache) & 15) || (reinterpret_cast<uintptr_t>(Ly.v_cache) & 15))
+            return record_error(HESA_CUDA_INVALID_ARGUMENT, "KV caches must be 16-byte aligned");
+        // q|k|v of this rank's heads (local)
+        cudaError_t e = qmv_strip_fused(qt, Ly.wq, qd_r + 2 * kd_r, D, x_own, SI::kRmsNorm, Ly.attn_norm, m->rms_eps,
+                                        q, nullptr, 1.0f, s);
+        if (e != cudaSuccess) return record_cuda_error(e, "sharded q|k|v");
+        // attention of this rank's heads -> every rank's a (barrier 1)
+        e = attention_rope_shard(q, k, v, Ly.k_cache, Ly.v_cache, nullptr, hl, kvl, HD, rope_table, rope_rows, m->ctx,
+                                 pos_dev, att_ws, a_out, W, ps, s);
+        if (e != cudaSuccess) return record_cuda_error(e, "sharded attention");
+        // x[d0:d1] += Wo a -> every rank's x (barrier 2)
+        rc = strip(Ly.wo, d1 - d0, QD, sh->a_peers[r], SI::kPlain, nullptr, x_own + d0,
+                   peers(sh->x_peers, d0, d1 - d0, nullptr, 0, 0));
+        // gate|up rows of this rank -> every rank's gate|up (barrier 3)
+        if (!rc)
+            rc = strip(Ly.w_gate, 2 * (f1 - f0), D, x_own, SI::kRmsNorm, Ly.ffn_norm, nullptr,
+                       peers(sh->gu_peers, f0, 2 * (f1 - f0), sh->gu_peers, F + f0, f1 - f0));
+        // x[d0:d1] += Wdown silu(g) u -> every rank's x (barrier 4)
+        if (!rc)
+            rc = strip(Ly.w_down, d1 - d0, F, sh->gu_peers[r], SI::kSiluMul, nullptr, x_own + d0,
+                       peers(sh->x_peers, d0, d1 - d0, nullptr, 0, 0));
+    }
+    if (!rc)
+        rc = strip(w_out, v1 - v0, D, x_own, SI::kRmsNorm, out_norm, nullptr,
+                   peers(sh->logits_peers, v0, v1 - v0, nullptr, 0, 0));
+    return rc;
+}

@@ -37,6 +37,7 @@
 #include "qmatvec.h"
 #include "xdigits.cuh"
 #include "strip_core.cuh"
+#include "peer_sync.cuh"
 
 #include <cuda/atomic>
 
@@ -351,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
                  float* __restrict__ y, float scale, int chunk_rows, int n_slots, int slot_stride, int rows_cap,
                  int xmode, const float* __restrict__ norm_w, float eps, const float* __restrict__ resid,
-                 PeerOut peer, int* __restrict__ status) {
+                 PeerOut peer, PeerSync sync, int* __restrict__ status) {
     constexpr int UB = unit_bytes(QT);
     extern __shared__ __align__(128) uint8_t smem[];
 
@@ -587,9 +588,16 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
             float s = 0.f;
             for (int t = 0; t < wps; ++t) s += part[i * wps + t];
-            const float val = s * scale;
-            for (int p = 0; p < peer.world; ++p) peer.y[par][p][r0 + i] = val;
+            const int row = r0 + i;
+            const float val = resid ? __fadd_rn(resid[row], s * scale) : s * scale;
+            for (int p = 0; p < peer.world; ++p) {
+                if (row < peer.split) peer.y[par][p][row] = val;
+                else peer.y2[par][p][row - peer.split] = val;
+            }
         }
+        // the sharded decode step: every rank's part is stored everywhere
+        // once the last CTA of this grid has heard from every rank
+        grid_end_peer_barrier(sync, status);
     }
 }
 
@@ -742,16 +750,18 @@ bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
 template <int QT>
 cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
                          const StripPlan& p, int xmode, const float* norm_w, float eps, const float* resid,
-                         const PeerOut& peer, cudaStream_t stream) {
+                         const PeerOut& peer, const PeerSync& sync, cudaStream_t stream) {
     static int smem_set[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (smem_set[dev] < kMaxSmem) {
-        e = cudaFuncSetAttribute(qmv_strip_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (smem_set[dev] < kStripSmemMax) {
+        // the plan's budget (the kernel's few bytes of static shared memory
+        // come on top, within the 227 KB a CTA may have)
+        e = cudaFuncSetAttribute(qmv_strip_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStripSmemMax);
         if (e != cudaSuccess) return e;
-        smem_set[dev] = kMaxSmem;
+        smem_set[dev] = kStripSmemMax;
     }
     int* status = nullptr;
     e = status_ptr(&status);
@@ -769,7 +779,7 @@ cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, flo
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, qmv_strip_kernel<QT>, w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
-                              p.slot_stride, p.rows_cap, xmode, norm_w, eps, resid, peer, status);
+                              p.slot_stride, p.rows_cap, xmode, norm_w, eps, resid, peer, sync, status);
 }
 
 template <int QT>
@@ -881,29 +891,55 @@ cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, 
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_out), kk = static_cast<int>(k);
     const PeerOut none = {};
+    const PeerSync nosync = {};
     switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, stream);
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
         default: return cudaErrorInvalidValue;
     }
 }
 
 cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
-                             const PeerOut& out, cudaStream_t stream) {
+                             const PeerOut& out_in, cudaStream_t stream) {
     StripPlan p;
-    if (!plan_strip(qtype, n_rows, k, p) || out.world < 1 || out.world > kMaxPeers || !out.epoch)
+    if (!plan_strip(qtype, n_rows, k, p) || out_in.world < 1 || out_in.world > kMaxPeers || !out_in.epoch)
         return cudaErrorInvalidValue;
+    PeerOut out = out_in;
+    out.split = static_cast<int>(n_rows);   // every row to y
+    const PeerSync nosync = {};
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
     switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, stream);
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, StripInput in,
+                            const float* norm_w, float eps, const float* resid, float scale, const PeerOut& out,
+                            const PeerSync& sync, cudaStream_t stream) {
+    StripPlan p;
+    if (!plan_strip(qtype, n_rows, k, p) || out.world < 1 || out.world > kMaxPeers || !out.epoch ||
+        sync.world != out.world || !sync.epoch || !sync.ticket)
+        return cudaErrorInvalidValue;
+    if (in == StripInput::kRmsNorm && (!norm_w || k > static_cast<int64_t>(kWarps) * kStripBatch * 256))
+        return cudaErrorInvalidValue;
+    const int xm = in == StripInput::kRmsNorm ? kXRmsNorm : in == StripInput::kSiluMul ? kXSiluMul : kXPlain;
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
+    switch (qtype) {
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -53,11 +53,28 @@ cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, 
 constexpr int kMaxPeers = 8;
 struct PeerOut {
     float* y[2][kMaxPeers];   // [parity][rank]: where this shard's row 0 lands in that rank's buffer
+    // rows >= split land in y2 instead (row `split` at y2[parity][rank]):
+    // a joined gate|up shard whose halves go to two places of the gathered
+    // vector; split = n_rows when unused
+    float* y2[2][kMaxPeers];
+    int split;
     const uint32_t* epoch;    // this rank's barrier count (device); parity = *epoch & 1
     int world;                // number of ranks; 0 = plain output
 };
 cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
                              const PeerOut& out, cudaStream_t stream);
+
+}  // namespace hesa_cuda
+#include "peer_sync.cuh"
+namespace hesa_cuda {
+
+// The strip kernel of the sharded decode step: y rows (with a transformed
+// input and an optional residual, as qmv_strip_fused) stored into every rank
+// through `out`, then the cross-rank barrier at the end of the grid (`sync`).
+// resid points at this shard's row 0 of the residual.
+cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, StripInput in,
+                            const float* norm_w, float eps, const float* resid, float scale, const PeerOut& out,
+                            const PeerSync& sync, cudaStream_t stream);
 
 // Completion of the fused all-gathers of one step: every rank publishes
 // *epoch + 1 into slot `rank` of every rank's flags (release, system scope),

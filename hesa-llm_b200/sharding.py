@@ -175,3 +175,101 @@ class GatheredQMatvec:
         self.launch(x, scale, stream)
         self.peers.barrier(stream)
         return self.peers.output(par)[self.row_offset:self.row_offset + self.n_out]
+
+
+class ShardedDecoder:
+    """One sequence decoded on `world` GPUs of a node (hesa_cuda_decode_step_sharded).
+
+    Rank r keeps the Q, K, V rows of heads [r*H/world, (r+1)*H/world) (and of
+    its kv heads), their KV caches, and its balanced row share (row_range) of
+    Wo, gate|up, W_down and the LM head; the attention output, both residual
+    updates and gate|up are gathered into every rank by the kernels that make
+    them, each grid ending with a cross-rank barrier (peer stores over NVLink,
+    CUDA IPC mappings exchanged through `group`).
+
+    full: the unsharded model on this rank's device, laid out as the decode
+    step takes it -- a dict with "layers" (dicts of CUDA tensors: wq/wk/wv
+    views of one joined Q|K|V allocation, w_gate/w_up of one gate|up
+    allocation, wo, w_down, attn_norm, ffn_norm, k_cache, v_cache [ctx, KD]
+    fp16), "w_out", "out_norm" and "table" (the device rope table).
+    """
+
+    FIELDS = ("x", "a", "gu", "logits", "flags", "epoch", "ticket")
+
+    def __init__(self, cfg: dict, full: dict, rank: int, world: int, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+        import hesa_cuda as H
+        self.cfg, self.rank, self.world = dict(cfg), rank, world
+        D, HD, F, V = cfg["d_model"], cfg["head_dim"], cfg["d_ff"], cfg["vocab"]
+        NH, NKV = cfg["n_head"], cfg["n_kv_head"]
+        if NH % world or NKV % world:
+            raise ValueError(f"n_head {NH} and n_kv_head {NKV} must be multiples of world {world}")
+        QD, KD = NH * HD, NKV * HD
+        qd_r, kd_r = QD // world, KD // world
+        d0, d1 = row_range(D, rank, world)
+        f0, f1 = row_range(F, rank, world)
+        v0, v1 = row_range(V, rank, world)
+        self.rows = dict(d=(d0, d1), f=(f0, f1), v=(v0, v1))
+        self.layers = []
+        for L in full["layers"]:
+            qkv = torch.cat([L["wq"][rank * qd_r:(rank + 1) * qd_r], L["wk"][rank * kd_r:(rank + 1) * kd_r],
+                             L["wv"][rank * kd_r:(rank + 1) * kd_r]]).contiguous()
+            gu = torch.cat([L["w_gate"][f0:f1], L["w_up"][f0:f1]]).contiguous()
+            kc = L["k_cache"][:, rank * kd_r:(rank + 1) * kd_r].contiguous()
+            vc = L["v_cache"][:, rank * kd_r:(rank + 1) * kd_r].contiguous()
+            self.layers.append(dict(wq=qkv[:qd_r], wk=qkv[qd_r:qd_r + kd_r], wv=qkv[qd_r + kd_r:],
+                                    wo=L["wo"][d0:d1].contiguous(), w_gate=gu[:f1 - f0], w_up=gu[f1 - f0:],
+                                    w_down=L["w_down"][d0:d1].contiguous(), attn_norm=L["attn_norm"],
+                                    ffn_norm=L["ffn_norm"], k_cache=kc, v_cache=vc, _keep=(qkv, gu)))
+        self.w_out = full["w_out"][v0:v1].contiguous()
+        self.out_norm, self.table = full["out_norm"], full["table"]
+        self.model = H.Model(cfg["n_layer"], D, NH, NKV, HD, F, V, cfg["ctx"], cfg["rms_eps"], cfg["rope_base"],
+                             cfg["qtype"])
+        self.arr = H.make_layers(self.layers)
+        self.ws = H.decode_workspace(self.model, device)
+        # one peer allocation per rank: x | a | gate,up | logits | flags | epoch | ticket
+        sizes = dict(x=4 * D, a=4 * QD, gu=8 * F, logits=4 * V, flags=4 * world, epoch=4, ticket=4)
+        self.off, total = {}, 0
+        for name in self.FIELDS:
+            self.off[name] = total
+            total += _align(sizes[name])
+        self.local, handle = H.peer_alloc(total)
+        handles = [handle]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle, group=group)
+        self.base = [self.local if p == rank else H.peer_open(handles[p]) for p in range(world)]
+        self.device = device
+        self.shard = H.Shard(rank, world, *[self._ptrs(n) for n in ("x", "a", "gu", "logits", "flags")],
+                             self.local + self.off["epoch"], self.local + self.off["ticket"])
+
+    def _ptrs(self, name):
+        import ctypes
+        arr = (ctypes.c_void_p * self.world)(*[b + self.off[name] for b in self.base])
+        setattr(self, "_arr_" + name, arr)   # keep it alive with the struct
+        return arr
+
+    def buffer(self, name: str, numel: int, dtype: str = "<f4"):
+        """This rank's gathered buffer `name` (a torch view of device memory)."""
+        import hesa_cuda as H
+        return H.device_view(self.local + self.off[name], numel, device=self.device, dtype=dtype)
+
+    def logits(self):
+        return self.buffer("logits", self.cfg["vocab"])
+
+    def step(self, x_embed, pos_dev, stream=None) -> None:
+        """One token: every rank calls it with the same embedding and position."""
+        import hesa_cuda as H
+        H.decode_step_sharded(self.model, self.shard, self.arr, self.out_norm, self.w_out, self.table, x_embed,
+                              pos_dev, self.ws, stream=stream)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then free this rank's (every rank, after a
+        collective barrier, once no kernel uses them)."""
+        import hesa_cuda as H
+        for p, b in enumerate(self.base):
+            if p != self.rank:
+                H.peer_close(b)
+        H.peer_free(self.local)
+        self.base = []
