@@ -287,11 +287,12 @@ struct AttnRope {
     int table_rows;
     int* status;
     // head-sharded decode: head h's output goes to peer_out[p] + h * head_dim
-    // on every rank p (this rank's first head's place in rank p's buffer),
-    // then the cross-rank barrier at the end of the grid; peer_world 0: out
-    float* peer_out[kPeerSyncMax];
+    // on every rank p (this rank's first head's place in rank p's buffer) as
+    // tagged words (peer_sync.cuh); peer_world 0: to out
+    uint64_t* peer_out[kPeerSyncMax];
     int peer_world;
-    PeerSync sync;
+    const uint32_t* ll_count;
+    uint32_t ll_lo;
 };
 
 template <int DPL, bool ROPE>  // dims per lane (head_dim / 32)
@@ -578,7 +579,8 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
                 if (ri.peer_world == 0) {
                     out[o] = a * inv;
                 } else {
-                    for (int p = 0; p < ri.peer_world; ++p) ri.peer_out[p][o] = a * inv;
+                    const uint32_t tag = ll_tag(ri.ll_count, ri.ll_lo);
+                    for (int p = 0; p < ri.peer_world; ++p) st_ll(ri.peer_out[p] + o, a * inv, tag);
                 }
             }
             if (lane == 0) {
@@ -587,7 +589,6 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
             }
         }
     }
-    if constexpr (ROPE) grid_end_peer_barrier(ri.sync, ri.status);   // no-op unless head-sharded
 }
 
 int grid_for(int64_t n, int threads, int cap = 148 * 8) {
@@ -758,17 +759,18 @@ cudaError_t attention_rope(const float* q, const float* k_new, const float* v_ne
                            int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
                            cudaStream_t s) {
     return attention_rope_shard(q, k_new, v_new, kc, vc, out, n_head, n_kv_head, head_dim, table, table_rows, ctx,
-                                pos_dev, workspace, nullptr, 0, PeerSync{}, s);
+                                pos_dev, workspace, nullptr, 0, nullptr, 0u, s);
 }
 
 cudaError_t attention_rope_shard(const float* q, const float* k_new, const float* v_new, void* kc, void* vc,
                                  float* out, int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
                                  int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
-                                 float* const* peer_out, int peer_world, const PeerSync& sync, cudaStream_t s) {
+                                 uint64_t* const* peer_out, int peer_world, const uint32_t* ll_count, uint32_t ll_lo,
+                                 cudaStream_t s) {
     int* status = nullptr;
     cudaError_t e = status_word(&status);
     if (e != cudaSuccess) return e;
-    if (peer_world < 0 || peer_world > kPeerSyncMax || (peer_world > 0 && (!peer_out || sync.world != peer_world)))
+    if (peer_world < 0 || peer_world > kPeerSyncMax || (peer_world > 0 && (!peer_out || !ll_count)))
         return cudaErrorInvalidValue;
     AttnRope ri = {};
     ri.k_new = k_new;
@@ -783,7 +785,8 @@ cudaError_t attention_rope_shard(const float* q, const float* k_new, const float
         if (!peer_out[p]) return cudaErrorInvalidValue;
         ri.peer_out[p] = peer_out[p];
     }
-    ri.sync = sync;
+    ri.ll_count = ll_count;
+    ri.ll_lo = ll_lo;
     return attention_any<true>(q, kc, vc, out, n_head, n_kv_head, head_dim, ctx, pos_dev, 0, workspace, ri, s);
 }
 

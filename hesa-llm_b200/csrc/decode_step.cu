@@ -26,6 +26,7 @@
 #include "qtypes.cuh"
 #include "peer_sync.cuh"
 
+#include <algorithm>
 #include <cstdint>
 
 namespace hesa_cuda {
@@ -261,24 +262,55 @@ int hesa_cuda_decode_step(const hesa_cuda_model* m, const hesa_cuda_layer* layer
 // head-sharded decode step
 // ---------------------------------------------------------------------------
 
+namespace hesa_cuda {
+namespace {
+
+// Tag low bits of the step's exchanges: (layer << 3) | phase.
+enum : uint32_t { kPhEmbed = 0, kPhAttn = 1, kPhWo = 2, kPhGateUp = 3, kPhDown = 4, kPhLogits = 5 };
+constexpr uint32_t lo_of(int64_t layer, uint32_t phase) { return (static_cast<uint32_t>(layer) << 3) | phase; }
+
+// The token's embedding into this rank's tagged residual buffer; opens the
+// token (one CTA: every thread reads the old count, then it is advanced).
+__global__ void __launch_bounds__(1024) ll_fill_kernel(const float* __restrict__ x, uint64_t* x_ll, int n,
+                                                       uint32_t* count) {
+    const uint32_t c = *reinterpret_cast<volatile uint32_t*>(count) + 1u;
+    const uint32_t tag = (c << 12) | lo_of(0, kPhEmbed);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) st_ll(x_ll + i, x[i], tag);
+    __syncthreads();
+    if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(count) = c;
+}
+
+// This rank's tagged logits into the caller's plain buffer.
+__global__ void ll_unpack_kernel(const uint64_t* ll, float* __restrict__ out, int n, const uint32_t* count,
+                                 uint32_t lo, unsigned long long limit_ns, int* status) {
+    const uint32_t tag = ll_tag(count, lo);
+    bool ok = true;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        out[i] = ld_ll_wait(ll + i, tag, limit_ns, status, ok);
+}
+
+}  // namespace
+}  // namespace hesa_cuda
+
 extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hesa_cuda_shard* sh,
                                              const hesa_cuda_layer* layers, const float* out_norm, const void* w_out,
                                              const float* rope_table, int32_t rope_rows, const float* x_embed,
-                                             const int32_t* pos_dev, void* workspace, size_t workspace_bytes,
-                                             void* stream) {
+                                             const int32_t* pos_dev, float* logits, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
     using namespace hesa_cuda;
     if (!model_ok(m)) return record_error(HESA_CUDA_SHAPE_MISMATCH, "bad model shape");
-    if (!sh || !layers || !out_norm || !w_out || !rope_table || !x_embed || !pos_dev || !workspace)
+    if (!sh || !layers || !out_norm || !w_out || !rope_table || !x_embed || !pos_dev || !logits || !workspace)
         return record_error(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     const int W = sh->world, r = sh->rank;
     if (W < 1 || W > kPeerSyncMax || r < 0 || r >= W) return record_error(HESA_CUDA_INVALID_ARGUMENT, "bad rank / world");
-    if (!sh->x_peers || !sh->a_peers || !sh->gu_peers || !sh->logits_peers || !sh->flags || !sh->epoch || !sh->ticket)
+    if (!sh->x_peers || !sh->a_peers || !sh->gu_peers || !sh->logits_peers || !sh->token_count)
         return record_error(HESA_CUDA_INVALID_ARGUMENT, "null shard buffer array");
     for (int p = 0; p < W; ++p)
-        if (!sh->x_peers[p] || !sh->a_peers[p] || !sh->gu_peers[p] || !sh->logits_peers[p] || !sh->flags[p])
+        if (!sh->x_peers[p] || !sh->a_peers[p] || !sh->gu_peers[p] || !sh->logits_peers[p])
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "null peer buffer");
     if (m->n_head % W != 0 || m->n_kv_head % W != 0)
         return record_error(HESA_CUDA_SHAPE_MISMATCH, "n_head and n_kv_head must be multiples of world");
+    if (m->n_layer >= 512) return record_error(HESA_CUDA_SHAPE_MISMATCH, "n_layer must be below 512");
     if (rope_rows <= 0) return record_error(HESA_CUDA_SHAPE_MISMATCH, "empty rope table");
     const Layout L = layout(m);
     if (workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255))
@@ -311,48 +343,57 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
         return record_error(HESA_CUDA_SHAPE_MISMATCH, "a shard does not fit the row-strip kernel");
     if ((HD != 64 && HD != 128 && HD != 256) || m->ctx > 131072)
         return record_error(HESA_CUDA_SHAPE_MISMATCH, "head_dim must be 64, 128 or 256, ctx <= 131072");
+    int* status = nullptr;
+    cudaError_t e = status_word(&status);
+    if (e != cudaSuccess) return record_cuda_error(e, "status word");
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     float* q = reinterpret_cast<float*>(ws + L.qkv);
     float* k = q + qd_r;
     float* v = k + kd_r;
     void* att_ws = ws + L.att;
-    float* x_own = sh->x_peers[r];
+    uint64_t* x_own = sh->x_peers[r];
+    const uint32_t* cnt = sh->token_count;
+    const unsigned long long limit_ns = peer_wait_limit();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-    PeerSync ps = {};
-    for (int p = 0; p < W; ++p) ps.flags[p] = sh->flags[p];
-    ps.epoch = sh->epoch;
-    ps.ticket = reinterpret_cast<int*>(sh->ticket);
-    ps.limit_ns = peer_wait_limit();
-    ps.rank = r;
-    ps.world = W;
-    // every gathered vector: this rank's part lands at `off` of every rank's buffer
-    auto peers = [&](float* const* bufs, int64_t off, int64_t n_rows, float* const* bufs2, int64_t off2,
-                     int64_t split) {
-        PeerOut o = {};
+    auto in = [&](const uint64_t* x, uint32_t x_lo, const uint64_t* resid, uint32_t resid_lo) {
+        LLIn li = {};
+        li.x = x;
+        li.resid = resid;
+        li.count = cnt;
+        li.x_lo = x_lo;
+        li.resid_lo = resid_lo;
+        li.limit_ns = limit_ns;
+        return li;
+    };
+    // this rank's part lands at `off` of every rank's buffer (rows from
+    // `split` on at off2 of bufs2)
+    auto out = [&](uint64_t* const* bufs, int64_t off, int64_t n_rows, uint64_t* const* bufs2, int64_t off2,
+                   int64_t split, uint32_t lo) {
+        LLOut o = {};
         for (int p = 0; p < W; ++p) {
-            o.y[0][p] = o.y[1][p] = bufs[p] + off;
-            o.y2[0][p] = o.y2[1][p] = bufs2 ? bufs2[p] + off2 : nullptr;
+            o.y[p] = bufs[p] + off;
+            o.y2[p] = bufs2 ? bufs2[p] + off2 : nullptr;
         }
         o.split = static_cast<int>(bufs2 ? split : n_rows);
-        o.epoch = sh->epoch;
         o.world = W;
+        o.count = cnt;
+        o.lo = lo;
         return o;
     };
-    auto strip = [&](const void* w, int64_t n, int64_t kk, const float* xin, SI in, const float* nw,
-                     const float* resid, const PeerOut& o) {
-        const cudaError_t e = qmv_strip_shard(qt, w, n, kk, xin, in, nw, m->rms_eps, resid, 1.0f, o, ps, s);
-        return e == cudaSuccess ? HESA_CUDA_OK : record_cuda_error(e, "sharded matvec");
+    auto strip = [&](const void* w, int64_t n, int64_t kk, SI mode, const float* nw, float* y, const LLIn& li,
+                     const LLOut& lo, const char* what) {
+        const cudaError_t ce = qmv_strip_shard(qt, w, n, kk, mode, nw, m->rms_eps, 1.0f, y, li, lo, s);
+        return ce == cudaSuccess ? HESA_CUDA_OK : record_cuda_error(ce, what);
     };
 
-    int rc = HESA_CUDA_OK;
-    if (x_embed != x_own) {
-        const cudaError_t ce = cudaMemcpyAsync(x_own, x_embed, D * 4, cudaMemcpyDeviceToDevice, s);
-        if (ce != cudaSuccess) rc = record_cuda_error(ce, "copy of the embedding");
-    }
-    float* a_out[kPeerSyncMax] = {};
+    ll_fill_kernel<<<1, 1024, 0, s>>>(x_embed, x_own, static_cast<int>(D), sh->token_count);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return record_cuda_error(e, "embedding fill");
+    uint64_t* a_out[kPeerSyncMax] = {};
     for (int p = 0; p < W; ++p) a_out[p] = sh->a_peers[p] + r * qd_r;
+    int rc = HESA_CUDA_OK;
     for (int l = 0; l < m->n_layer && rc == HESA_CUDA_OK; ++l) {
         const hesa_cuda_layer& Ly = layers[l];
         if (!Ly.wq || !Ly.wk || !Ly.wv || !Ly.wo || !Ly.w_gate || !Ly.w_up || !Ly.w_down || !Ly.attn_norm ||
@@ -364,28 +405,42 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "Q|K|V and gate|up shards must be joined");
         if ((reinterpret_cast<uintptr_t>(Ly.k_cache) & 15) || (reinterpret_cast<uintptr_t>(Ly.v_cache) & 15))
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "KV caches must be 16-byte aligned");
+        // the residual as the previous exchange left it
+        const uint32_t x_lo = l == 0 ? lo_of(0, kPhEmbed) : lo_of(l - 1, kPhDown);
         // q|k|v of this rank's heads (local)
-        cudaError_t e = qmv_strip_fused(qt, Ly.wq, qd_r + 2 * kd_r, D, x_own, SI::kRmsNorm, Ly.attn_norm, m->rms_eps,
-                                        q, nullptr, 1.0f, s);
-        if (e != cudaSuccess) return record_cuda_error(e, "sharded q|k|v");
-        // attention of this rank's heads -> every rank's a (barrier 1)
+        rc = strip(Ly.wq, qd_r + 2 * kd_r, D, SI::kRmsNorm, Ly.attn_norm, q, in(x_own, x_lo, nullptr, 0), LLOut{},
+                   "sharded q|k|v");
+        if (rc) break;
+        // attention of this rank's heads -> every rank's a
         e = attention_rope_shard(q, k, v, Ly.k_cache, Ly.v_cache, nullptr, hl, kvl, HD, rope_table, rope_rows, m->ctx,
-                                 pos_dev, att_ws, a_out, W, ps, s);
+                                 pos_dev, att_ws, a_out, W, cnt, lo_of(l, kPhAttn), s);
         if (e != cudaSuccess) return record_cuda_error(e, "sharded attention");
-        // x[d0:d1] += Wo a -> every rank's x (barrier 2)
-        rc = strip(Ly.wo, d1 - d0, QD, sh->a_peers[r], SI::kPlain, nullptr, x_own + d0,
-                   peers(sh->x_peers, d0, d1 - d0, nullptr, 0, 0));
-        // gate|up rows of this rank -> every rank's gate|up (barrier 3)
+        // x[d0:d1] += Wo a -> every rank's x
+        rc = strip(Ly.wo, d1 - d0, QD, SI::kPlain, nullptr, nullptr,
+                   in(sh->a_peers[r], lo_of(l, kPhAttn), x_own + d0, x_lo),
+                   out(sh->x_peers, d0, d1 - d0, nullptr, 0, 0, lo_of(l, kPhWo)), "sharded Wo");
+        // gate|up rows of this rank -> every rank's gate|up
         if (!rc)
-            rc = strip(Ly.w_gate, 2 * (f1 - f0), D, x_own, SI::kRmsNorm, Ly.ffn_norm, nullptr,
-                       peers(sh->gu_peers, f0, 2 * (f1 - f0), sh->gu_peers, F + f0, f1 - f0));
-        // x[d0:d1] += Wdown silu(g) u -> every rank's x (barrier 4)
+            rc = strip(Ly.w_gate, 2 * (f1 - f0), D, SI::kRmsNorm, Ly.ffn_norm, nullptr,
+                       in(x_own, lo_of(l, kPhWo), nullptr, 0),
+                       out(sh->gu_peers, f0, 2 * (f1 - f0), sh->gu_peers, F + f0, f1 - f0, lo_of(l, kPhGateUp)),
+                       "sharded gate|up");
+        // x[d0:d1] += Wdown silu(g) u -> every rank's x
         if (!rc)
-            rc = strip(Ly.w_down, d1 - d0, F, sh->gu_peers[r], SI::kSiluMul, nullptr, x_own + d0,
-                       peers(sh->x_peers, d0, d1 - d0, nullptr, 0, 0));
+            rc = strip(Ly.w_down, d1 - d0, F, SI::kSiluMul, nullptr, nullptr,
+                       in(sh->gu_peers[r], lo_of(l, kPhGateUp), x_own + d0, lo_of(l, kPhWo)),
+                       out(sh->x_peers, d0, d1 - d0, nullptr, 0, 0, lo_of(l, kPhDown)), "sharded W_down");
     }
+    const int64_t NL = m->n_layer;
     if (!rc)
-        rc = strip(w_out, v1 - v0, D, x_own, SI::kRmsNorm, out_norm, nullptr,
-                   peers(sh->logits_peers, v0, v1 - v0, nullptr, 0, 0));
+        rc = strip(w_out, v1 - v0, D, SI::kRmsNorm, out_norm, nullptr, in(x_own, lo_of(NL - 1, kPhDown), nullptr, 0),
+                   out(sh->logits_peers, v0, v1 - v0, nullptr, 0, 0, lo_of(NL, kPhLogits)), "sharded LM head");
+    if (!rc) {
+        const int grid = static_cast<int>(std::min<int64_t>((V + 255) / 256, 148));
+        ll_unpack_kernel<<<grid, 256, 0, s>>>(sh->logits_peers[r], logits, static_cast<int>(V), cnt,
+                                              lo_of(NL, kPhLogits), limit_ns, status);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) rc = record_cuda_error(e, "logits unpack");
+    }
     return rc;
 }

@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
                  float* __restrict__ y, float scale, int chunk_rows, int n_slots, int slot_stride, int rows_cap,
                  int xmode, const float* __restrict__ norm_w, float eps, const float* __restrict__ resid,
-                 PeerOut peer, PeerSync sync, int* __restrict__ status) {
+                 PeerOut peer, LLIn lin, LLOut lout, int* __restrict__ status) {
     constexpr int UB = unit_bytes(QT);
     extern __shared__ __align__(128) uint8_t smem[];
 
@@ -433,6 +433,9 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     // (measured: 9.25 vs 10.45 us for a 4096x11008 Q4_K launch).
     if (threadIdx.x == 0) issue(0);
     grid_dep_wait();
+    // tagged inputs (sharded decode step): the tags of this token
+    bool ll_ok = true;
+    const uint32_t x_tag = lin.x ? ll_tag(lin.count, lin.x_lo) : 0u;
 
     // x as digit planes, converted once per CTA (one warp per unit of 256;
     // the loads of a batch of units are issued together). The input may be
@@ -442,10 +445,10 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     if (xmode == kXRmsNorm) {
         float v[kStripBatch][8];
         float ss = 0.f;
+        if (lin.x) load8_ll_batch(lin.x, x_tag, lin.limit_ns, warp, lane, U, v, status, ll_ok);
 #pragma unroll
         for (int jb = 0; jb < kStripBatch; ++jb) {
-            const int u = warp + jb * kWarps;
-            load8(x, u, lane, U, v[jb]);
+            if (!lin.x) load8(x, warp + jb * kWarps, lane, U, v[jb]);
 #pragma unroll
             for (int j = 0; j < 8; ++j) ss = fmaf(v[jb][j], v[jb][j], ss);
         }
@@ -470,18 +473,27 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     } else {
         for (int ub = warp; ub < U; ub += kWarps * kStripBatch) {
             float v[kStripBatch][8];
+            if (lin.x) {
+                load8_ll_batch(lin.x, x_tag, lin.limit_ns, ub, lane, U, v, status, ll_ok);
+                if (xmode == kXSiluMul) {
+                    float up[kStripBatch][8];
+                    load8_ll_batch(lin.x + k, x_tag, lin.limit_ns, ub, lane, U, up, status, ll_ok);
 #pragma unroll
-            for (int jb = 0; jb < kStripBatch; ++jb) {
-                const int u = ub + jb * kWarps;
-                load8(x, u, lane, U, v[jb]);
-                if (xmode == kXSiluMul && u < U) {
-                    // the value is rounded to 22 bits below its unit's maximum right
-                    // after, so the fast exp and divide (a few ulp) change nothing
-                    // that survives that rounding
-                    float up[8];
-                    load8(x + k, u, lane, U, up);
+                    for (int jb = 0; jb < kStripBatch; ++jb)
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) v[jb][j] = __fdividef(v[jb][j], 1.0f + __expf(-v[jb][j])) * up[j];
+                        for (int j = 0; j < 8; ++j) v[jb][j] = swiglu_x(v[jb][j], up[jb][j]);
+                }
+            } else {
+#pragma unroll
+                for (int jb = 0; jb < kStripBatch; ++jb) {
+                    const int u = ub + jb * kWarps;
+                    load8(x, u, lane, U, v[jb]);
+                    if (xmode == kXSiluMul && u < U) {
+                        float up[8];
+                        load8(x + k, u, lane, U, up);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) v[jb][j] = swiglu_x(v[jb][j], up[j]);
+                    }
                 }
             }
 #pragma unroll
@@ -570,7 +582,23 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         }
         return;
     }
-    if (peer.world == 0) {
+    if (lout.world > 0) {
+        // sharded decode step: every row to every rank, tagged with this
+        // token's place in the step
+        const uint32_t tag = ll_tag(lout.count, lout.lo);
+        const uint32_t rtag = lin.resid ? ll_tag(lin.count, lin.resid_lo) : 0u;
+        for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
+            float s = 0.f;
+            for (int t = 0; t < wps; ++t) s += part[i * wps + t];
+            const int row = r0 + i;
+            const float val = lin.resid ? __fadd_rn(ld_ll_wait(lin.resid + row, rtag, lin.limit_ns, status, ll_ok), s * scale)
+                                        : s * scale;
+            for (int p = 0; p < lout.world; ++p) {
+                if (row < lout.split) st_ll(lout.y[p] + row, val, tag);
+                else st_ll(lout.y2[p] + (row - lout.split), val, tag);
+            }
+        }
+    } else if (peer.world == 0) {
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
             float s = 0.f;
             for (int t = 0; t < wps; ++t) s += part[i * wps + t];
@@ -595,9 +623,6 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
                 else peer.y2[par][p][row - peer.split] = val;
             }
         }
-        // the sharded decode step: every rank's part is stored everywhere
-        // once the last CTA of this grid has heard from every rank
-        grid_end_peer_barrier(sync, status);
     }
 }
 
@@ -750,7 +775,7 @@ bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
 template <int QT>
 cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
                          const StripPlan& p, int xmode, const float* norm_w, float eps, const float* resid,
-                         const PeerOut& peer, const PeerSync& sync, cudaStream_t stream) {
+                         const PeerOut& peer, const LLIn& lin, const LLOut& lout, cudaStream_t stream) {
     static int smem_set[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -779,7 +804,7 @@ cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, flo
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, qmv_strip_kernel<QT>, w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
-                              p.slot_stride, p.rows_cap, xmode, norm_w, eps, resid, peer, sync, status);
+                              p.slot_stride, p.rows_cap, xmode, norm_w, eps, resid, peer, lin, lout, status);
 }
 
 template <int QT>
@@ -891,13 +916,14 @@ cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, 
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_out), kk = static_cast<int>(k);
     const PeerOut none = {};
-    const PeerSync nosync = {};
+    const LLIn nolin = {};
+    const LLOut nolout = {};
     switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nosync, stream);
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -909,25 +935,24 @@ cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k
         return cudaErrorInvalidValue;
     PeerOut out = out_in;
     out.split = static_cast<int>(n_rows);   // every row to y
-    const PeerSync nosync = {};
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
     switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, nosync, stream);
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
         default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, StripInput in,
-                            const float* norm_w, float eps, const float* resid, float scale, const PeerOut& out,
-                            const PeerSync& sync, cudaStream_t stream) {
+cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, StripInput in, const float* norm_w,
+                            float eps, float scale, float* y, const LLIn& lin, const LLOut& lout,
+                            cudaStream_t stream) {
     StripPlan p;
-    if (!plan_strip(qtype, n_rows, k, p) || out.world < 1 || out.world > kMaxPeers || !out.epoch ||
-        sync.world != out.world || !sync.epoch || !sync.ticket)
+    if (!plan_strip(qtype, n_rows, k, p) || !lin.x || !lin.count || lout.world < 0 || lout.world > kPeerSyncMax ||
+        (lout.world > 0 && !lout.count) || (lout.world == 0 && (!y || lin.resid)))
         return cudaErrorInvalidValue;
     if (in == StripInput::kRmsNorm && (!norm_w || k > static_cast<int64_t>(kWarps) * kStripBatch * 256))
         return cudaErrorInvalidValue;
@@ -935,11 +960,11 @@ cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k,
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
     switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, resid, out, sync, stream);
+        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
+        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
+        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
+        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
+        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
         default: return cudaErrorInvalidValue;
     }
 }

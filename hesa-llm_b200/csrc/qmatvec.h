@@ -68,13 +68,13 @@ cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k
 #include "peer_sync.cuh"
 namespace hesa_cuda {
 
-// The strip kernel of the sharded decode step: y rows (with a transformed
-// input and an optional residual, as qmv_strip_fused) stored into every rank
-// through `out`, then the cross-rank barrier at the end of the grid (`sync`).
-// resid points at this shard's row 0 of the residual.
-cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, StripInput in,
-                            const float* norm_w, float eps, const float* resid, float scale, const PeerOut& out,
-                            const PeerSync& sync, cudaStream_t stream);
+// The strip kernel of the sharded decode step: rows of y = scale * W . f(x)
+// (+ the residual) from tagged inputs (lin: x, and the residual when set) to
+// every rank as tagged words (lout), or, when lout.world is 0, to the plain
+// local y (no residual); f as qmv_strip_fused.
+cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, StripInput in, const float* norm_w,
+                            float eps, float scale, float* y, const LLIn& lin, const LLOut& lout,
+                            cudaStream_t stream);
 
 // Completion of the fused all-gathers of one step: every rank publishes
 // *epoch + 1 into slot `rank` of every rank's flags (release, system scope),

@@ -18,6 +18,7 @@
 #include "hesa_common.cuh"
 #include "qtypes.cuh"
 #include "xdigits.cuh"
+#include "peer_sync.cuh"
 
 namespace hesa_cuda {
 namespace strip {
@@ -330,6 +331,37 @@ __device__ __forceinline__ void load8(const float* __restrict__ src, int u, int 
     } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    }
+}
+
+// silu(g) * u for the SwiGLU input. The value is rounded to 22 bits below its
+// unit's maximum right after, so the fast exp and divide (a few ulp) change
+// nothing that survives that rounding.
+__device__ __forceinline__ float swiglu_x(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
+
+// load8 from a tagged vector (peer_sync.cuh), each value once its tag is
+// `tag`, for the kStripBatch units u0 + jb * kWarps: the loads of two units
+// are issued before the first of their tags is looked at (more would spill).
+__device__ __forceinline__ void load8_ll_batch(const uint64_t* src, uint32_t tag, unsigned long long limit_ns, int u0,
+                                               int lane, int U, float (&v)[kStripBatch][8], int* status, bool& ok) {
+#pragma unroll
+    for (int jh = 0; jh < kStripBatch; jh += 2) {
+        uint64_t w[2][8];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int u = u0 + (jh + i) * kWarps;
+            if (u < U) ld_ll8_issue(src + static_cast<size_t>(u) * 256 + lane * 8, w[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int u = u0 + (jh + i) * kWarps;
+            if (u < U) {
+                ld_ll8_take(src + static_cast<size_t>(u) * 256 + lane * 8, w[i], tag, limit_ns, v[jh + i], status, ok);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[jh + i][j] = 0.f;
+            }
+        }
     }
 }
 

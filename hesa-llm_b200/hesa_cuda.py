@@ -77,7 +77,7 @@ SIGNATURES = [
     ("hesa_cuda_peer_barrier", _int, [ctypes.POINTER(_vp), _int, _int, _vp, _vp]),
     ("hesa_cuda_set_peer_wait_limit_us", _int, [ctypes.c_uint32]),
     ("hesa_cuda_decode_step_sharded", _int, [ctypes.POINTER(Model), _vp, ctypes.POINTER(Layer), _vp, _vp, _vp,
-                                             ctypes.c_int32, _vp, _vp, _vp, _sz, _vp]),
+                                             ctypes.c_int32, _vp, _vp, _vp, _vp, _sz, _vp]),
 ]
 
 
@@ -85,12 +85,11 @@ class Shard(ctypes.Structure):
     """hesa_cuda_shard (include/hesa_cuda.h): one rank of a head-sharded decode."""
     _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("x_peers", ctypes.c_void_p),
                 ("a_peers", ctypes.c_void_p), ("gu_peers", ctypes.c_void_p), ("logits_peers", ctypes.c_void_p),
-                ("flags", ctypes.c_void_p), ("epoch", ctypes.c_void_p), ("ticket", ctypes.c_void_p)]
+                ("token_count", ctypes.c_void_p)]
 
-    def __init__(self, rank, world, x, a, gu, logits, flags, epoch, ticket):
+    def __init__(self, rank, world, x, a, gu, logits, token_count):
         super().__init__(rank, world, ctypes.cast(x, ctypes.c_void_p), ctypes.cast(a, ctypes.c_void_p),
-                         ctypes.cast(gu, ctypes.c_void_p), ctypes.cast(logits, ctypes.c_void_p),
-                         ctypes.cast(flags, ctypes.c_void_p), epoch, ticket)
+                         ctypes.cast(gu, ctypes.c_void_p), ctypes.cast(logits, ctypes.c_void_p), token_count)
 
 
 class HesaError(RuntimeError):
@@ -410,14 +409,14 @@ def decode_step(model: Model, layers, out_norm, w_out, rope_table, x_embed, pos_
     return logits
 
 
-def decode_step_sharded(model: Model, shard, layers, out_norm, w_out, rope_table, x_embed, pos_dev, workspace,
-                        stream=None):
-    """This rank's part of one token of a head-sharded decode (hesa_cuda_decode_step_sharded);
-    the logits arrive in every rank's logits buffer."""
+def decode_step_sharded(model: Model, shard, layers, out_norm, w_out, rope_table, x_embed, pos_dev, logits,
+                        workspace, stream=None):
+    """This rank's part of one token of a head-sharded decode
+    (hesa_cuda_decode_step_sharded); every rank gets all the logits."""
     _check(lib().hesa_cuda_decode_step_sharded(ctypes.byref(model), ctypes.byref(shard), layers, out_norm.data_ptr(),
                                                w_out.data_ptr(), rope_table.data_ptr(), rope_table.shape[0],
-                                               x_embed.data_ptr(), pos_dev.data_ptr(), workspace.data_ptr(),
-                                               workspace.numel(), _stream_handle(stream)))
+                                               x_embed.data_ptr(), pos_dev.data_ptr(), logits.data_ptr(),
+                                               workspace.data_ptr(), workspace.numel(), _stream_handle(stream)))
 
 
 def make_layers(per_layer):

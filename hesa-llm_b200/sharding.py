@@ -184,8 +184,8 @@ class ShardedDecoder:
     its kv heads), their KV caches, and its balanced row share (row_range) of
     Wo, gate|up, W_down and the LM head; the attention output, both residual
     updates and gate|up are gathered into every rank by the kernels that make
-    them, each grid ending with a cross-rank barrier (peer stores over NVLink,
-    CUDA IPC mappings exchanged through `group`).
+    them, as tagged 64-bit words that the consuming kernels wait for (peer
+    stores over NVLink, CUDA IPC mappings exchanged through `group`).
 
     full: the unsharded model on this rank's device, laid out as the decode
     step takes it -- a dict with "layers" (dicts of CUDA tensors: wq/wk/wv
@@ -194,7 +194,7 @@ class ShardedDecoder:
     fp16), "w_out", "out_norm" and "table" (the device rope table).
     """
 
-    FIELDS = ("x", "a", "gu", "logits", "flags", "epoch", "ticket")
+    FIELDS = ("x", "a", "gu", "logits", "count")
 
     def __init__(self, cfg: dict, full: dict, rank: int, world: int, group=None, device=None):
         import torch
@@ -228,8 +228,9 @@ class ShardedDecoder:
                              cfg["qtype"])
         self.arr = H.make_layers(self.layers)
         self.ws = H.decode_workspace(self.model, device)
-        # one peer allocation per rank: x | a | gate,up | logits | flags | epoch | ticket
-        sizes = dict(x=4 * D, a=4 * QD, gu=8 * F, logits=4 * V, flags=4 * world, epoch=4, ticket=4)
+        # one peer allocation per rank: tagged words (8 bytes) of x | a | gate,up
+        # | logits, then the token counter
+        sizes = dict(x=8 * D, a=8 * QD, gu=16 * F, logits=8 * V, count=4)
         self.off, total = {}, 0
         for name in self.FIELDS:
             self.off[name] = total
@@ -241,8 +242,9 @@ class ShardedDecoder:
             dist.all_gather_object(handles, handle, group=group)
         self.base = [self.local if p == rank else H.peer_open(handles[p]) for p in range(world)]
         self.device = device
-        self.shard = H.Shard(rank, world, *[self._ptrs(n) for n in ("x", "a", "gu", "logits", "flags")],
-                             self.local + self.off["epoch"], self.local + self.off["ticket"])
+        self.shard = H.Shard(rank, world, *[self._ptrs(n) for n in ("x", "a", "gu", "logits")],
+                             self.local + self.off["count"])
+        self.out = torch.empty(V, dtype=torch.float32, device=device)
 
     def _ptrs(self, name):
         import ctypes
@@ -250,19 +252,15 @@ class ShardedDecoder:
         setattr(self, "_arr_" + name, arr)   # keep it alive with the struct
         return arr
 
-    def buffer(self, name: str, numel: int, dtype: str = "<f4"):
-        """This rank's gathered buffer `name` (a torch view of device memory)."""
-        import hesa_cuda as H
-        return H.device_view(self.local + self.off[name], numel, device=self.device, dtype=dtype)
-
     def logits(self):
-        return self.buffer("logits", self.cfg["vocab"])
+        """All the logits of the last step (this rank's device memory)."""
+        return self.out
 
     def step(self, x_embed, pos_dev, stream=None) -> None:
         """One token: every rank calls it with the same embedding and position."""
         import hesa_cuda as H
         H.decode_step_sharded(self.model, self.shard, self.arr, self.out_norm, self.w_out, self.table, x_embed,
-                              pos_dev, self.ws, stream=stream)
+                              pos_dev, self.out, self.ws, stream=stream)
 
     def close(self) -> None:
         """Unmap the peers' buffers, then free this rank's (every rank, after a

@@ -274,45 +274,48 @@ HESA_CUDA_API int hesa_cuda_decode_step(const hesa_cuda_model* model, const hesa
  * [ctx, n_kv_head/world * head_dim], and its balanced row share of Wo, of
  * gate|up (joined: its up rows right after its gate rows), of W_down and of
  * the LM head (rows [floor(r*n/world), floor((r+1)*n/world)) of each). Every
- * rank keeps the full residual vector x. Per layer the attention output, the
+ * rank keeps the full residual vector. Per layer the attention output, the
  * Wo residual, gate|up and the W_down residual are gathered: the kernel that
  * produces each stores its part straight into every rank's buffer over
- * NVLink and its grid ends with a bounded cross-rank barrier (device status
- * 4 when a peer does not arrive in time; see hesa_cuda_set_peer_wait_limit_us).
- * The buffers are peer allocations (hesa_cuda_peer_alloc / _open); arrays
- * are host arrays of `world` device pointers, entry p = rank p's buffer as
- * mapped in this process. The decomposition of the reference's decode loop
- * (docs/architecture.md:277-281) over the GPUs of one node; no counterpart in
- * the reference, which runs on one device. */
+ * NVLink, every value as one 64-bit word with a tag naming the token and the
+ * place in the step, and the kernel that consumes it reads each word once its
+ * tag is the expected one (bounded wait: device status 4 when a peer does not
+ * deliver in time) -- no fence, flag array or barrier launch per exchange.
+ * The buffers are peer allocations (hesa_cuda_peer_alloc / _open) of 8 bytes
+ * per element; arrays are host arrays of `world` device pointers, entry p =
+ * rank p's buffer as mapped in this process. The decomposition of the
+ * reference's decode loop (docs/architecture.md:277-281) over the GPUs of one
+ * node; no counterpart in the reference, which runs on one device. */
 typedef struct {
     int32_t rank, world;
-    float* const* x_peers;       /* [d_model] residual vectors */
-    float* const* a_peers;       /* [n_head * head_dim] attention outputs */
-    float* const* gu_peers;      /* [2 * d_ff] gate | up */
-    float* const* logits_peers;  /* [vocab] */
-    uint32_t* const* flags;      /* [world] uint32 flag arrays, zero-initialised */
-    uint32_t* epoch;             /* this rank's barrier count (device uint32, zero-initialised) */
-    int32_t* ticket;             /* this rank's arrival counter (device int32, zero-initialised) */
+    uint64_t* const* x_peers;       /* [d_model] the residual vector */
+    uint64_t* const* a_peers;       /* [n_head * head_dim] attention outputs */
+    uint64_t* const* gu_peers;      /* [2 * d_ff] gate | up */
+    uint64_t* const* logits_peers;  /* [vocab] */
+    uint32_t* token_count;          /* this rank's token counter (device uint32, zero-initialised) */
 } hesa_cuda_shard;
 
 /* One token of the decoder on this rank: `layers` hold this rank's shards,
  * w_out its LM-head rows; x_embed the token's embedding (the same on every
- * rank). The logits arrive in logits_peers[rank] (all of them, on every
- * rank). Every rank must issue the same steps; the workspace is
+ * rank); logits [vocab] (this rank's device memory) receives all the logits.
+ * Every rank must issue the same steps; the workspace is
  * hesa_cuda_decode_workspace_size(model) bytes (model = the full, unsharded
- * shape). n_head and n_kv_head must be multiples of world; the shards must
- * fit the row-strip kernel (k <= 24576; d_model <= 12288). */
+ * shape). n_head and n_kv_head must be multiples of world, n_layer < 512; the
+ * shards must fit the row-strip kernel (k <= 24576; d_model <= 12288). Each
+ * word a peer delivers is waited for at most the peer wait limit
+ * (hesa_cuda_set_peer_wait_limit_us, read when the step is enqueued). */
 HESA_CUDA_API int hesa_cuda_decode_step_sharded(const hesa_cuda_model* model, const hesa_cuda_shard* shard,
                                                 const hesa_cuda_layer* layers, const float* out_norm,
                                                 const void* w_out, const float* rope_table, int32_t rope_rows,
-                                                const float* x_embed, const int32_t* pos_dev, void* workspace,
-                                                size_t workspace_bytes, void* stream);
+                                                const float* x_embed, const int32_t* pos_dev, float* logits,
+                                                void* workspace, size_t workspace_bytes, void* stream);
 
 /* Sticky device-side status of the kernels: 0 while nothing has gone wrong
  * in this process, else the first code recorded: 1 a bulk copy did not land
  * within the bounded wait, 2 a copy was still in flight when the kernel
  * gave up, 3 a device-side position outside the KV cache or the rope table,
- * 4 a peer rank did not reach hesa_cuda_peer_barrier in time.
+ * 4 a peer rank did not reach hesa_cuda_peer_barrier, or did not deliver a
+ * word of the sharded decode step, in time.
  * Reading synchronizes `stream`. hesa_cuda_clear_device_status resets it. */
 HESA_CUDA_API int hesa_cuda_device_status(void* stream, int* status_out);
 
@@ -364,8 +367,8 @@ HESA_CUDA_API int hesa_cuda_peer_barrier(uint32_t* const* flags, int rank, int w
 
 /* How long each wait for a peer rank lasts (hesa_cuda_peer_barrier) before it
  * gives up, records device status 4 and returns, in microseconds; 0 restores
- * the default of 2 s, values above 60 s are refused. Applies to barriers
- * enqueued after the call (a CUDA graph keeps the limit it was captured
+ * the default of 2 s, values above 60 s are refused. Applies to barriers and
+ * sharded decode steps enqueued after the call (a CUDA graph keeps the limit it was captured
  * with). The host-side counterpart of a collective timeout: a rank that
  * dies between steps costs its peers at most this long per barrier, and the
  * status word tells them why. No counterpart in the reference (one device). */

@@ -1,7 +1,7 @@
 """One sequence decoded on several GPUs (hesa_cuda_decode_step_sharded,
 sharding.ShardedDecoder): heads, their KV caches and row shares of Wo,
-gate|up, W_down and the LM head per rank; the gathers fused into the kernels
-that produce each vector, each grid ending in a bounded cross-rank barrier.
+gate|up, W_down and the LM head per rank; every kernel stores its rows into
+every rank as tagged 64-bit words and the next kernel waits per word (bounded).
 
 World 1 (one GPU): the sharded step's logits are bit-identical to the
 unsharded decode step's and within rel-L2 1e-5 of the oracle, for
