@@ -21,10 +21,11 @@ Metric: algorithmic bytes (packed W + x + y) per second, whole job.
 N > 1 GPUs (torchrun): weak scaling with row-sharded weights -- rank r holds
 rows [r*n, (r+1)*n) of an N-times taller matrix (its shard has the N=1 shape)
 and every rank ends each step holding the full outputs: the matvec kernels
-store their rows straight into every rank's gathered buffer over NVLink
-(hesa_cuda_qmatvec_gather) and one barrier kernel per step publishes
-completion (hesa_cuda_peer_barrier). The same step with an NCCL all-gather
-instead is timed beside it ("nccl_allgather").
+store their rows straight into every rank's gathered buffer over NVLink as
+tagged 64-bit words (hesa_cuda_qmatvec_gather_tagged) and one collector kernel
+per step waits until every word of this rank's buffer carries the step's tag
+(hesa_cuda_peer_collect). The same step with an NCCL all-gather instead is
+timed beside it ("nccl_allgather").
 
 --impl reference: times the reference CPU path (above) on rank 0 only.
 """
@@ -477,37 +478,57 @@ def proj70b_bytes(world: int) -> int:
     return sum(n * row_bytes(qt, k) + 4 * k * world + 4 * n for _, n, k in PROJ70B)
 
 
-def run_proj70b(dev, stream, rank: int, world: int, reps: int = 20):
+def run_proj70b(dev, stream, rank: int, world: int, pg=None, reps: int = 20):
     """70B-shaped Q4_K projections (d_model 8192, FFN 28672, 8 KV heads of
     128), batch 1, row-sharded: this rank holds rows [r0, r1) of each of the
     seven matrices (sharding.row_range) and one pass is its seven matvecs,
-    replayed from a CUDA graph (443 MB of weights at N = 1, more than L2).
-    Returns ms per pass on this rank (device time)."""
+    replayed from a CUDA graph (443 MB of weights at N = 1, more than L2). At
+    N > 1 every pass also gathers the seven outputs on every rank (tagged peer
+    stores from the matvecs, one collector per pass). Returns (ms per pass with
+    the gather, ms per pass of the local matvecs alone) on this rank (device
+    time)."""
     import torch
     import hesa_cuda as H
     import sharding
     qt = QT["Q4_K"]
     g = torch.Generator(device=dev)
     g.manual_seed(7070 + rank)
+    tg = sharding.TaggedGather(sum(n for _, n, _ in PROJ70B), rank, world, device=dev) if world > 1 else None
     mats = []
+    off = 0
     for name, n, k in PROJ70B:
         r0, r1 = sharding.row_range(n, rank, world)
         w = H.quantize(qt, torch.randn((r1 - r0, k), generator=g, device=dev) * 0.02)
         x = torch.randn(k, generator=g, device=dev)
         y = torch.empty(r1 - r0, device=dev)
-        mats.append((w, x, y, H.make_workspace(qt, r1 - r0, k, device=dev)))
-    with torch.cuda.stream(stream):
-        def one():
-            for w, x, y, ws in mats:
-                H.qmatvec(qt, w, x, y=y, workspace=ws, stream=stream)
-        one()
+        # the gather's workspace: only the down projection (k = 28672, longer
+        # rows than the strip kernel takes) needs one
+        gws = H.gather_tagged_workspace(qt, r1 - r0, k, device=dev) if tg else None
+        mats.append((w, x, y, H.make_workspace(qt, r1 - r0, k, device=dev), tg.targets(off + r0) if tg else None,
+                     gws))
+        off += n
+
+    def local():
+        for w, x, y, ws, t, gws in mats:
+            H.qmatvec(qt, w, x, y=y, workspace=ws, stream=stream)
+
+    def gathered():
+        for w, x, y, ws, t, gws in mats:
+            H.qmatvec_gather_tagged(qt, w, x, t, world, tg.sync, workspace=gws, stream=stream)
+        tg.collect(stream=stream)
+
+    def timed(body):
+        body()
         stream.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            one()
+            body()
         for _ in range(3):
             graph.replay()
         stream.synchronize()
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -515,9 +536,18 @@ def run_proj70b(dev, stream, rank: int, world: int, reps: int = 20):
             graph.replay()
         e1.record(stream)
         e1.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    del graph, mats
-    return ms
+        del graph
+        return e0.elapsed_time(e1) / reps
+
+    with torch.cuda.stream(stream):
+        ms_local = timed(local)
+        ms = timed(gathered) if tg is not None else ms_local
+    if tg is not None:
+        torch.cuda.synchronize(dev)
+        pg.barrier()
+        tg.close()
+    del mats
+    return ms, ms_local
 
 
 def run_decode(dev, stream, steps: int, warmup: int, pg=None, rank: int = 0, world: int = 1):
@@ -534,14 +564,23 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None, rank: int = 0, wor
     pos_dev = torch.tensor([DECODE_POS], dtype=torch.int32, device=dev)
     tok_dev = torch.tensor([1234], dtype=torch.int32, device=dev)
     dec = None
+    want = None
     if world > 1:
         import sharding
+        # the unsharded step on this rank's full copy: the sharded step computes
+        # every row with the same summation order, so its logits must equal
+        # these bit for bit
+        H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok_dev, out=x, stream=stream)
+        want = torch.empty_like(logits)
+        H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos_dev, want, d["ws"],
+                      stream=stream)
+        stream.synchronize()
         dec = sharding.ShardedDecoder(cfg, d, rank, world, device=dev)
         logits = dec.logits()
         del d["layers"], d["arr"]   # the full model's weights: every rank keeps its shards only
         torch.cuda.empty_cache()
         torch.cuda.synchronize(dev)
-        pg.barrier()   # the ranks meet their first peer barrier within its wait limit
+        pg.barrier()   # the ranks start their first step within the peer wait limit of one another
 
     def step():
         H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok_dev, out=x, stream=stream)
@@ -573,13 +612,14 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None, rank: int = 0, wor
         e1.synchronize()
         ms = e0.elapsed_time(e1) / steps
     ok = bool(torch.isfinite(logits).all().item()) and H.device_status(stream) == 0
+    same = None if want is None else bool(torch.equal(logits, want))
     del graph
     if dec is not None:
         torch.cuda.synchronize(dev)
         pg.barrier()
         dec.close()
         pg.barrier()
-    return dict(ms=ms, finite=ok, bytes_token=d["bytes_token"], weight_bytes=d["weight_bytes"],
+    return dict(ms=ms, finite=ok, equal_unsharded=same, bytes_token=d["bytes_token"], weight_bytes=d["weight_bytes"],
                 kv_bytes=d["kv_bytes"])
 
 
@@ -666,16 +706,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         # gathered buffers shared over NVLink, laid out as NCCL's all-gather of
         # y_local lays them out: rank r's block of all eight outputs at r * rows
         import sharding
-        peers = sharding.PeerGather(y_all.numel(), rank, world, device=dev)
+        peers = sharding.TaggedGather(y_all.numel(), rank, world, device=dev)
         off = rank * y_local.numel()
         for name, qt, n, k, wt, xt, yt, ws in dmats:
             targets.append(peers.targets(off))
             off += n
         pg.barrier()
-
-    def barrier_count():
-        torch.cuda.synchronize(dev)
-        return int(H.device_view(peers.epoch, 1, device=dev, dtype="<i4")[0])
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -695,8 +731,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         if peers is None:
             return one_step_nccl()
         for (name, qt, n, k, wt, xt, yt, ws), tgt in zip(dmats, targets):
-            H.qmatvec_gather(qt, wt, xt, tgt, world, peers.epoch, stream=stream)
-        H.peer_barrier(peers.flags, rank, world, peers.epoch, stream=stream)
+            H.qmatvec_gather_tagged(qt, wt, xt, tgt, world, peers.sync, stream=stream)
+        peers.collect(stream=stream)
 
     if args.profile:
         # a short, untimed run for ncu: K plain steps (8 launches each), no graphs
@@ -727,8 +763,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         sampler = ClockSampler(local_rank) if rank == 0 else None
         if sampler:
             sampler.start()
-        # the same number of replays on every rank (each step ends in a
-        # cross-rank barrier), sized to ~2 s from a short timed run
+        # the same number of replays on every rank (each step ends waiting for
+        # every rank's rows), sized to ~2 s from a short timed run
         t0 = time.time()
         for _ in range(50):
             graph.replay()
@@ -844,8 +880,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         h2d = x_host.numel() * 4
         d2h = y_host.numel() * 4
 
-        def e2e_body(parity=0):
-            # parity: which of the two gathered buffers this step fills (N > 1)
+        def e2e_body():
             x_all.copy_(x_host, non_blocking=True)
             if peers is None:
                 off = 0
@@ -855,13 +890,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                 y_host.copy_(y_out, non_blocking=True)
             else:
                 one_step()
-                y_host.copy_(peers.output(parity), non_blocking=True)
-
-        count = [barrier_count() if peers is not None else 0]
+                y_host.copy_(peers.out, non_blocking=True)
 
         def e2e_step():
-            e2e_body(count[0] & 1)
-            count[0] += 1
+            e2e_body()
             stream.synchronize()
 
         # eager: every call from Python, as a notebook user would make them
@@ -880,15 +912,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
         # graphed: the same public-API calls and copies captured once, as a
         # serving loop runs its decode step; each replay copies x in from
-        # pinned host memory and y back out, and the host waits for it. At
-        # N > 1 a replay holds two steps, one per gathered buffer, so the
-        # buffer each copy reads stays the one its step filled.
-        per_replay = 1 if peers is None else 2
+        # pinned host memory and y back out, and the host waits for it
+        per_replay = 1
         g_e2e = torch.cuda.CUDAGraph()
-        p0 = count[0] & 1
         with torch.cuda.graph(g_e2e, stream=stream):
-            for j in range(per_replay):
-                e2e_body((p0 + j) & 1)
+            e2e_body()
         for _ in range(3):
             g_e2e.replay()
             stream.synchronize()
@@ -904,22 +932,25 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         e2e_ms = ee0.elapsed_time(ee1) * args.steps / (replays * per_replay)
         if peers is not None:
             # the gathered outputs equal the NCCL-gathered ones
+            one_step()
             one_step_nccl()
             stream.synchronize()
-            par = (barrier_count() - 1) & 1
-            gathered_ok = bool(torch.equal(peers.output(par), y_all))
+            gathered_ok = bool(torch.equal(peers.out, y_all))
 
-    # the 7B-shaped Q4_K decode step, one full replica per rank
+    # the 7B-shaped Q4_K decode step of one sequence (sharded over the ranks at N > 1)
     dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg, rank=rank, world=world)
     batched = run_batched(dev, stream) if rank == 0 else None
-    p70_ms = run_proj70b(dev, stream, rank, world)
+    p70_ms, p70_local_ms = run_proj70b(dev, stream, rank, world, pg=pg)
 
     # max over ranks
     times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec["ms"], nccl_ms or 0.0,
-                          0.0 if peers is None or gathered_ok else 1.0, p70_ms], dtype=torch.float64, device=dev)
+                          0.0 if peers is None or gathered_ok else 1.0, p70_ms,
+                          0.0 if dec["equal_unsharded"] in (None, True) else 1.0, p70_local_ms],
+                         dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
-    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms, nccl_ms, gather_bad, p70_ms = (float(v) for v in times.cpu())
+    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms, nccl_ms, gather_bad, p70_ms, dec_bad, p70_local_ms = (
+        float(v) for v in times.cpu())
 
     if rank == 0:
         bytes_step = step_bytes() * world
@@ -937,7 +968,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                    "([n_out x k]), batch 1",
                        "bytes_per_step_per_gpu": step_bytes(), "l2": L2_NOTE,
                        "parallelism": (f"row-sharded weights x{world}, all-gather of y fused into the matvec "
-                                       "(peer stores over NVLink + one barrier kernel per step)" if world > 1
+                                       "(tagged peer stores over NVLink + one collector kernel per step)"
+                                       if world > 1
                                        else "single GPU"),
                        "timing": "CUDA graph of one step, replayed K times between CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -953,7 +985,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             "pct_of_8tbs": round(achieved / 8000.0, 4),
             "e2e": {"value": round(bytes_step * args.steps / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-                    "how": "hesa_cuda.qmatvec per matrix (hesa_cuda.qmatvec_gather + peer_barrier at N > 1); "
+                    "how": "hesa_cuda.qmatvec per matrix (hesa_cuda.qmatvec_gather_tagged + peer_collect at "
+                           "N > 1); "
                            "every step one copy of all activations from pinned host memory and one copy of "
                            "all outputs back, captured once in a CUDA graph and replayed with a host "
                            "synchronize per replay",
@@ -968,11 +1001,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                        "frac_of_hbm": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9 / (peak * world), 4),
                        "parallelism": (f"one sequence on {world} GPUs: heads, KV caches and row shares of every "
                                        "projection per rank, the four gathers per layer fused into the kernels "
-                                       "(peer stores + a barrier at the end of each grid)" if world > 1
-                                       else "single GPU"),
+                                       "(tagged 64-bit peer stores, waited for per word by the next kernel)"
+                                       if world > 1 else "single GPU"),
                        "timing": "embedding lookup + 32 layers + LM head captured as one CUDA graph per token, "
                                  "replayed between CUDA events",
-                       "logits_finite": dec["finite"]},
+                       "logits_finite": dec["finite"],
+                       "logits_equal_unsharded_step": (dec_bad == 0.0) if world > 1 else None},
             "batched": {"workload": "Q4_K [n_out x k] times B activation rows (batched decode), "
                                     "one launch per 16 rows on the tensor cores (B >= 3; B = 2 as two batch-1 passes)",
                         "us_and_gbs": batched,
@@ -980,10 +1014,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             "proj70b": {"workload": "70B-shaped Q4_K projections, batch 1: Wq, Wo 8192x8192; Wk, Wv 1024x8192; "
                                    "gate, up 28672x8192; down 8192x28672 ([n_out x k])",
                         "parallelism": (f"rows split over {world} GPUs (each rank its shards; time = max over "
-                                        "ranks; outputs stay on their rank, the fused gather is timed in the "
-                                        "sweep line)" if world > 1 else "single GPU"),
+                                        "ranks), every rank ends each pass with all seven full outputs (tagged "
+                                        "peer stores from the matvecs + one collector per pass)"
+                                        if world > 1 else "single GPU"),
                         "scaling": "strong",
                         "ms_per_pass": round(p70_ms, 4),
+                        "ms_per_pass_without_gather": round(p70_local_ms, 4),
                         "gbs": round(proj70b_bytes(world) / (p70_ms * 1e-3) / 1e9, 1),
                         "bytes_per_pass": proj70b_bytes(world),
                         "timing": "the seven matvecs in one CUDA graph, 20 replays between CUDA events"},

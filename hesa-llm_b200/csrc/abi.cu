@@ -191,6 +191,72 @@ int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_rows, int64_t k
     return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "gathered matvec kernel");
 }
 
+// Low bits of the tagged gather's tags: never 0, so the zero-filled words of a
+// fresh allocation never pass for step 0's.
+constexpr uint32_t kGatherTagLo = 1;
+
+size_t hesa_cuda_gather_tagged_workspace_size(int qtype, int64_t n_rows, int64_t k) {
+    if (!hesa_cuda::qtype_supported(qtype) || n_rows <= 0 || k <= 0 || k % 256 != 0) return 0;
+    if (hesa_cuda::qmv_strip_shape_ok(qtype, n_rows, k)) return 0;
+    // the plain matvec's workspace, then its output [n_rows] (256-byte aligned)
+    const size_t mv = (hesa_cuda_qmatvec_workspace_size(qtype, n_rows, k, 1) + 255) & ~size_t(255);
+    return mv + ((static_cast<size_t>(n_rows) * 4 + 255) & ~size_t(255));
+}
+
+int hesa_cuda_qmatvec_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x,
+                                    float scale, uint64_t* const* y_peers, int world, const uint32_t* sync,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
+    if (!w || !x || !y_peers || !sync) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (world < 1 || world > hesa_cuda::kMaxPeers) return fail(HESA_CUDA_INVALID_ARGUMENT, "world must be 1..8");
+    if (n_rows <= 0 || k <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "non-positive dimension");
+    if (n_rows >= (int64_t(1) << 30) || k % 256 != 0)
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "gathered matvec needs k a multiple of 256");
+    if (!aligned16(w) || !aligned16(x)) return fail(HESA_CUDA_INVALID_ARGUMENT, "W and x must be 16-byte aligned");
+    const bool strip = hesa_cuda::qmv_strip_eligible(qtype, w, n_rows, k);
+    const size_t need = strip ? 0 : hesa_cuda_gather_tagged_workspace_size(qtype, n_rows, k);
+    if (!strip && (!workspace || workspace_bytes < need || !aligned16(workspace)))
+        return fail(HESA_CUDA_INVALID_ARGUMENT,
+                    "this shape needs a workspace of hesa_cuda_gather_tagged_workspace_size bytes");
+    hesa_cuda::LLOut out = {};
+    for (int b = 0; b < 2; ++b)
+        for (int p = 0; p < world; ++p) {
+            uint64_t* q = y_peers[b * world + p];
+            if (!q) return fail(HESA_CUDA_INVALID_ARGUMENT, "null output pointer");
+            if (reinterpret_cast<uintptr_t>(q) & 7) return fail(HESA_CUDA_INVALID_ARGUMENT, "outputs must be 8-byte aligned");
+            (b == 0 ? out.y : out.y2)[p] = q;
+        }
+    out.world = world;
+    out.by_parity = 1;
+    out.count = sync;
+    out.lo = kGatherTagLo;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (strip) {
+        const cudaError_t e = hesa_cuda::qmv_strip_gather_tagged(qtype, w, n_rows, k, x, scale, out, s);
+        return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "tagged gathered matvec kernel");
+    }
+    // rows longer than the strip kernel takes: the plain matvec into the
+    // workspace, then one kernel sends its rows to every rank
+    const size_t mv = need - ((static_cast<size_t>(n_rows) * 4 + 255) & ~size_t(255));
+    float* y_local = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + mv);
+    const int rc = hesa_cuda_qmatvec(qtype, w, n_rows, k, x, k, 1, y_local, n_rows, scale, workspace, mv, stream);
+    if (rc != HESA_CUDA_OK) return rc;
+    const cudaError_t e = hesa_cuda::peer_scatter_tagged(y_local, n_rows, out, s);
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "tagged scatter kernel");
+}
+
+int hesa_cuda_peer_collect(const uint64_t* words, int64_t n, int64_t parity_stride, float* out, uint32_t* sync,
+                           void* stream) {
+    if (!words || !out || !sync) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (n <= 0 || n >= (int64_t(1) << 30)) return fail(HESA_CUDA_SHAPE_MISMATCH, "word count must be 1 .. 2^30 - 1");
+    if (parity_stride < n) return fail(HESA_CUDA_SHAPE_MISMATCH, "the two parities overlap");
+    if ((reinterpret_cast<uintptr_t>(words) & 7) || (reinterpret_cast<uintptr_t>(sync) & 7))
+        return fail(HESA_CUDA_INVALID_ARGUMENT, "words and sync must be 8-byte aligned");
+    const cudaError_t e = hesa_cuda::peer_collect(words, words + parity_stride, n, out, sync, kGatherTagLo,
+                                                  static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "peer collect kernel");
+}
+
 int hesa_cuda_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch, void* stream) {
     if (!flags || !epoch) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (world < 1 || world > hesa_cuda::kMaxPeers || rank < 0 || rank >= world)

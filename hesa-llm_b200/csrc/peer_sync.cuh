@@ -90,11 +90,14 @@ struct LLIn {
 };
 
 // Tagged outputs: row i of this shard goes to y[p] + i of every rank p (rows
-// from `split` on to y2[p] + (i - split)).
+// from `split` on to y2[p] + (i - split)); with by_parity set, every row goes
+// to y[p] + i while the count is even and to y2[p] + i while it is odd (two
+// buffers a step apart, so a rank may store step s + 1 while a peer still
+// collects step s).
 struct LLOut {
     uint64_t* y[kPeerSyncMax];
     uint64_t* y2[kPeerSyncMax];
-    int split, world;
+    int split, world, by_parity;
     const uint32_t* count;
     uint32_t lo;
 };

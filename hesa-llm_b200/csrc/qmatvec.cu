@@ -347,7 +347,13 @@ constexpr int kStripMaxSlots = 16;
 
 constexpr int kStripSmemMax = 226 * 1024;
 
-template <int QT>
+// Where a strip kernel's rows go: the plain local y, every rank's gathered
+// buffer (PeerOut), or every rank as tagged words (LLOut). Each destination,
+// and a tagged input (LLX), is its own instantiation, so the plain matvec
+// carries none of the others' code or registers.
+enum : int { kOutPlain = 0, kOutPeer = 1, kOutTagged = 2 };
+
+template <int QT, bool LLX, int OUT>
 __global__ void __launch_bounds__(kThreads, 1)
 qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* __restrict__ x,
                  float* __restrict__ y, float scale, int chunk_rows, int n_slots, int slot_stride, int rows_cap,
@@ -435,7 +441,8 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     grid_dep_wait();
     // tagged inputs (sharded decode step): the tags of this token
     bool ll_ok = true;
-    const uint32_t x_tag = lin.x ? ll_tag(lin.count, lin.x_lo) : 0u;
+    uint32_t x_tag = 0;
+    if constexpr (LLX) x_tag = ll_tag(lin.count, lin.x_lo);
 
     // x as digit planes, converted once per CTA (one warp per unit of 256;
     // the loads of a batch of units are issued together). The input may be
@@ -445,12 +452,19 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     if (xmode == kXRmsNorm) {
         float v[kStripBatch][8];
         float ss = 0.f;
-        if (lin.x) load8_ll_batch(lin.x, x_tag, lin.limit_ns, warp, lane, U, v, status, ll_ok);
+        if constexpr (LLX) {
+            load8_ll_batch(lin.x, x_tag, lin.limit_ns, warp, lane, U, v, status, ll_ok);
 #pragma unroll
-        for (int jb = 0; jb < kStripBatch; ++jb) {
-            if (!lin.x) load8(x, warp + jb * kWarps, lane, U, v[jb]);
+            for (int jb = 0; jb < kStripBatch; ++jb)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) ss = fmaf(v[jb][j], v[jb][j], ss);
+                for (int j = 0; j < 8; ++j) ss = fmaf(v[jb][j], v[jb][j], ss);
+        } else {
+#pragma unroll
+            for (int jb = 0; jb < kStripBatch; ++jb) {
+                load8(x, warp + jb * kWarps, lane, U, v[jb]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss = fmaf(v[jb][j], v[jb][j], ss);
+            }
         }
         ss = warp_sum_f(ss);
         if (lane == 0) red[warp] = ss;
@@ -473,7 +487,7 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     } else {
         for (int ub = warp; ub < U; ub += kWarps * kStripBatch) {
             float v[kStripBatch][8];
-            if (lin.x) {
+            if constexpr (LLX) {
                 load8_ll_batch(lin.x, x_tag, lin.limit_ns, ub, lane, U, v, status, ll_ok);
                 if (xmode == kXSiluMul) {
                     float up[kStripBatch][8];
@@ -582,23 +596,28 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         }
         return;
     }
-    if (lout.world > 0) {
-        // sharded decode step: every row to every rank, tagged with this
-        // token's place in the step
+    if constexpr (OUT == kOutTagged) {
+        // every row to every rank, tagged with this step's place (sharded
+        // decode step, tagged gather)
         const uint32_t tag = ll_tag(lout.count, lout.lo);
-        const uint32_t rtag = lin.resid ? ll_tag(lin.count, lin.resid_lo) : 0u;
+        uint32_t rtag = 0;
+        if constexpr (LLX) rtag = lin.resid ? ll_tag(lin.count, lin.resid_lo) : 0u;
+        const bool odd = lout.by_parity && ((tag >> 12) & 1u);
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
             float s = 0.f;
             for (int t = 0; t < wps; ++t) s += part[i * wps + t];
             const int row = r0 + i;
-            const float val = lin.resid ? __fadd_rn(ld_ll_wait(lin.resid + row, rtag, lin.limit_ns, status, ll_ok), s * scale)
-                                        : s * scale;
+            float val = s * scale;
+            if constexpr (LLX) {
+                if (lin.resid) val = __fadd_rn(ld_ll_wait(lin.resid + row, rtag, lin.limit_ns, status, ll_ok), val);
+            }
             for (int p = 0; p < lout.world; ++p) {
-                if (row < lout.split) st_ll(lout.y[p] + row, val, tag);
+                if (lout.by_parity) st_ll((odd ? lout.y2[p] : lout.y[p]) + row, val, tag);
+                else if (row < lout.split) st_ll(lout.y[p] + row, val, tag);
                 else st_ll(lout.y2[p] + (row - lout.split), val, tag);
             }
         }
-    } else if (peer.world == 0) {
+    } else if constexpr (OUT == kOutPlain) {
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
             float s = 0.f;
             for (int t = 0; t < wps; ++t) s += part[i * wps + t];
@@ -616,12 +635,8 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
             float s = 0.f;
             for (int t = 0; t < wps; ++t) s += part[i * wps + t];
-            const int row = r0 + i;
-            const float val = resid ? __fadd_rn(resid[row], s * scale) : s * scale;
-            for (int p = 0; p < peer.world; ++p) {
-                if (row < peer.split) peer.y[par][p][row] = val;
-                else peer.y2[par][p][row - peer.split] = val;
-            }
+            const float val = s * scale;
+            for (int p = 0; p < peer.world; ++p) peer.y[par][p][r0 + i] = val;
         }
     }
 }
@@ -772,7 +787,7 @@ bool plan_strip(int qt, int64_t n_out, int64_t k, StripPlan& p) {
     return false;
 }
 
-template <int QT>
+template <int QT, bool LLX, int OUT>
 cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
                          const StripPlan& p, int xmode, const float* norm_w, float eps, const float* resid,
                          const PeerOut& peer, const LLIn& lin, const LLOut& lout, cudaStream_t stream) {
@@ -784,7 +799,7 @@ cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, flo
     if (smem_set[dev] < kStripSmemMax) {
         // the plan's budget (the kernel's few bytes of static shared memory
         // come on top, within the 227 KB a CTA may have)
-        e = cudaFuncSetAttribute(qmv_strip_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStripSmemMax);
+        e = cudaFuncSetAttribute(qmv_strip_kernel<QT, LLX, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStripSmemMax);
         if (e != cudaSuccess) return e;
         smem_set[dev] = kStripSmemMax;
     }
@@ -803,8 +818,23 @@ cudaError_t launch_strip(const uint8_t* w, int n_out, int k, const float* x, flo
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, qmv_strip_kernel<QT>, w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
+    return cudaLaunchKernelEx(&cfg, qmv_strip_kernel<QT, LLX, OUT>, w, n_out, k, x, y, scale, p.chunk_rows, p.n_slots,
                               p.slot_stride, p.rows_cap, xmode, norm_w, eps, resid, peer, lin, lout, status);
+}
+
+// launch_strip for a runtime quant type
+template <bool LLX, int OUT>
+cudaError_t launch_strip_qt(int qtype, const uint8_t* w, int n_out, int k, const float* x, float* y, float scale,
+                            const StripPlan& p, int xmode, const float* norm_w, float eps, const float* resid,
+                            const PeerOut& peer, const LLIn& lin, const LLOut& lout, cudaStream_t stream) {
+    switch (qtype) {
+        case kQ4_0: return launch_strip<kQ4_0, LLX, OUT>(w, n_out, k, x, y, scale, p, xmode, norm_w, eps, resid, peer, lin, lout, stream);
+        case kQ8_0: return launch_strip<kQ8_0, LLX, OUT>(w, n_out, k, x, y, scale, p, xmode, norm_w, eps, resid, peer, lin, lout, stream);
+        case kQ4_K: return launch_strip<kQ4_K, LLX, OUT>(w, n_out, k, x, y, scale, p, xmode, norm_w, eps, resid, peer, lin, lout, stream);
+        case kQ5_K: return launch_strip<kQ5_K, LLX, OUT>(w, n_out, k, x, y, scale, p, xmode, norm_w, eps, resid, peer, lin, lout, stream);
+        case kQ6_K: return launch_strip<kQ6_K, LLX, OUT>(w, n_out, k, x, y, scale, p, xmode, norm_w, eps, resid, peer, lin, lout, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 template <int QT>
@@ -890,9 +920,13 @@ cudaError_t qmv_stream(int qtype, const void* w, int64_t n_out, int64_t k, const
     }
 }
 
-bool qmv_strip_eligible(int qtype, const void* w, int64_t n_out, int64_t k) {
+bool qmv_strip_shape_ok(int qtype, int64_t n_out, int64_t k) {
     StripPlan p;
-    return (reinterpret_cast<uintptr_t>(w) % 16 == 0) && n_out < (int64_t(1) << 30) && plan_strip(qtype, n_out, k, p);
+    return n_out < (int64_t(1) << 30) && plan_strip(qtype, n_out, k, p);
+}
+
+bool qmv_strip_eligible(int qtype, const void* w, int64_t n_out, int64_t k) {
+    return (reinterpret_cast<uintptr_t>(w) % 16 == 0) && qmv_strip_shape_ok(qtype, n_out, k);
 }
 
 cudaError_t qmv_strip(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y, float scale,
@@ -915,17 +949,8 @@ cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, 
     const int xm = in == StripInput::kRmsNorm ? kXRmsNorm : in == StripInput::kSiluMul ? kXSiluMul : kXPlain;
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_out), kk = static_cast<int>(k);
-    const PeerOut none = {};
-    const LLIn nolin = {};
-    const LLOut nolout = {};
-    switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, none, nolin, nolout, stream);
-        default: return cudaErrorInvalidValue;
-    }
+    return launch_strip_qt<false, kOutPlain>(qtype, wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, PeerOut{},
+                                             LLIn{}, LLOut{}, stream);
 }
 
 cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
@@ -933,18 +958,10 @@ cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k
     StripPlan p;
     if (!plan_strip(qtype, n_rows, k, p) || out_in.world < 1 || out_in.world > kMaxPeers || !out_in.epoch)
         return cudaErrorInvalidValue;
-    PeerOut out = out_in;
-    out.split = static_cast<int>(n_rows);   // every row to y
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
-    switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr, out, LLIn{}, LLOut{}, stream);
-        default: return cudaErrorInvalidValue;
-    }
+    return launch_strip_qt<false, kOutPeer>(qtype, wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr,
+                                            out_in, LLIn{}, LLOut{}, stream);
 }
 
 cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, StripInput in, const float* norm_w,
@@ -959,14 +976,23 @@ cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k,
     const int xm = in == StripInput::kRmsNorm ? kXRmsNorm : in == StripInput::kSiluMul ? kXSiluMul : kXPlain;
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
-    switch (qtype) {
-        case kQ4_0: return launch_strip<kQ4_0>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
-        case kQ8_0: return launch_strip<kQ8_0>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
-        case kQ4_K: return launch_strip<kQ4_K>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
-        case kQ5_K: return launch_strip<kQ5_K>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
-        case kQ6_K: return launch_strip<kQ6_K>(wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr, PeerOut{}, lin, lout, stream);
-        default: return cudaErrorInvalidValue;
-    }
+    if (lout.world > 0)
+        return launch_strip_qt<true, kOutTagged>(qtype, wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr,
+                                                 PeerOut{}, lin, lout, stream);
+    return launch_strip_qt<true, kOutPlain>(qtype, wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr,
+                                            PeerOut{}, lin, lout, stream);
+}
+
+cudaError_t qmv_strip_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
+                                    const LLOut& lout, cudaStream_t stream) {
+    StripPlan p;
+    if (!plan_strip(qtype, n_rows, k, p) || !x || lout.world < 1 || lout.world > kPeerSyncMax || !lout.count ||
+        !lout.by_parity)
+        return cudaErrorInvalidValue;
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
+    return launch_strip_qt<false, kOutTagged>(qtype, wb, n, kk, x, nullptr, scale, p, kXPlain, nullptr, 0.f, nullptr,
+                                              PeerOut{}, LLIn{}, lout, stream);
 }
 
 cudaError_t qmv_rowwise(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,

@@ -31,6 +31,7 @@ cudaError_t qmv_stream_noalloc(int qtype, const void* w, int64_t n_out, int64_t 
 
 // Row-strip batch-1 matvec (k <= 24576): CTAs own contiguous rows, no workspace.
 bool qmv_strip_eligible(int qtype, const void* w, int64_t n_out, int64_t k);
+bool qmv_strip_shape_ok(int qtype, int64_t n_out, int64_t k);   // the same for a 16-byte aligned W
 cudaError_t qmv_strip(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, float* y, float scale,
                       cudaStream_t stream);
 
@@ -53,11 +54,6 @@ cudaError_t qmv_strip_fused(int qtype, const void* w, int64_t n_out, int64_t k, 
 constexpr int kMaxPeers = 8;
 struct PeerOut {
     float* y[2][kMaxPeers];   // [parity][rank]: where this shard's row 0 lands in that rank's buffer
-    // rows >= split land in y2 instead (row `split` at y2[parity][rank]):
-    // a joined gate|up shard whose halves go to two places of the gathered
-    // vector; split = n_rows when unused
-    float* y2[2][kMaxPeers];
-    int split;
     const uint32_t* epoch;    // this rank's barrier count (device); parity = *epoch & 1
     int world;                // number of ranks; 0 = plain output
 };
@@ -75,6 +71,27 @@ namespace hesa_cuda {
 cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, StripInput in, const float* norm_w,
                             float eps, float scale, float* y, const LLIn& lin, const LLOut& lout,
                             cudaStream_t stream);
+
+// Row-sharded matvec whose rows reach every rank as tagged words: row i to
+// lout.y[p] + i (lout.y2[p] + i while the count is odd; lout.by_parity must be
+// set) with the tag (*lout.count << 12) | lout.lo. x is a plain local vector.
+cudaError_t qmv_strip_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
+                                    const LLOut& lout, cudaStream_t stream);
+
+// y[0..n) (a plain local vector) to every rank as tagged words, as
+// qmv_strip_gather_tagged stores its rows; for shapes the strip kernel does
+// not take.
+cudaError_t peer_scatter_tagged(const float* y, int64_t n, const LLOut& lout, cudaStream_t stream);
+
+// End of a step of tagged gathers on this rank: waits (bounded by the peer
+// wait limit; kStatusPeerTimeout on expiry) until each of the n words of this
+// rank's buffer of the step's parity (words0 while sync[0] is even, words1
+// while odd) carries the tag (sync[0] << 12) | lo, writes their values to
+// out, then advances sync[0]. sync[1] is the launch's CTA ticket (zero between
+// launches). Launched with programmatic serialization; it waits for the grids
+// before it.
+cudaError_t peer_collect(const uint64_t* words0, const uint64_t* words1, int64_t n, float* out, uint32_t* sync,
+                         uint32_t lo, cudaStream_t stream);
 
 // Completion of the fused all-gathers of one step: every rank publishes
 // *epoch + 1 into slot `rank` of every rank's flags (release, system scope),

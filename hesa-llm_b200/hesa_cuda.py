@@ -75,6 +75,10 @@ SIGNATURES = [
     ("hesa_cuda_peer_close", _int, [_vp]),
     ("hesa_cuda_qmatvec_gather", _int, [_int, _vp, _i64, _i64, _vp, _f, ctypes.POINTER(_vp), _int, _vp, _vp]),
     ("hesa_cuda_peer_barrier", _int, [ctypes.POINTER(_vp), _int, _int, _vp, _vp]),
+    ("hesa_cuda_gather_tagged_workspace_size", _sz, [_int, _i64, _i64]),
+    ("hesa_cuda_qmatvec_gather_tagged", _int, [_int, _vp, _i64, _i64, _vp, _f, ctypes.POINTER(_vp), _int, _vp, _vp,
+                                               _sz, _vp]),
+    ("hesa_cuda_peer_collect", _int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     ("hesa_cuda_set_peer_wait_limit_us", _int, [ctypes.c_uint32]),
     ("hesa_cuda_decode_step_sharded", _int, [ctypes.POINTER(Model), _vp, ctypes.POINTER(Layer), _vp, _vp, _vp,
                                              ctypes.c_int32, _vp, _vp, _vp, _vp, _sz, _vp]),
@@ -233,6 +237,41 @@ def qmatvec_gather(qtype: int, w, x, y_peers, world: int, epoch: int, scale: flo
     arr = (ctypes.c_void_p * (2 * world))(*y_peers)
     _check(lib().hesa_cuda_qmatvec_gather(qtype, w.data_ptr(), n_rows, k, x.data_ptr(), float(scale), arr, world,
                                           epoch, _stream_handle(stream)))
+
+
+def gather_tagged_workspace(qtype: int, n_rows: int, k: int, device=None):
+    """The workspace qmatvec_gather_tagged needs for this shape (None when the
+    row-strip kernel takes it and none is needed)."""
+    import torch
+    nbytes = lib().hesa_cuda_gather_tagged_workspace_size(qtype, n_rows, k)
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device or "cuda") if nbytes else None
+
+
+def qmatvec_gather_tagged(qtype: int, w, x, y_peers, world: int, sync: int, scale: float = 1.0, workspace=None,
+                          stream=None):
+    """As qmatvec_gather, every row stored as a tagged 64-bit word; y_peers
+    lists 2 * world device addresses (parity-major) of this shard's first word
+    in each rank's buffers; sync is the device address of this rank's
+    [step count, ticket] pair. The step ends with peer_collect. Rows longer
+    than the strip kernel takes need `workspace` (gather_tagged_workspace)."""
+    n_rows, k = w.shape[0], x.shape[-1]
+    if workspace is None and lib().hesa_cuda_gather_tagged_workspace_size(qtype, n_rows, k):
+        workspace = gather_tagged_workspace(qtype, n_rows, k, device=x.device)
+    arr = (ctypes.c_void_p * (2 * world))(*y_peers)
+    _check(lib().hesa_cuda_qmatvec_gather_tagged(qtype, w.data_ptr(), n_rows, k, x.data_ptr(), float(scale), arr,
+                                                 world, sync, workspace.data_ptr() if workspace is not None else None,
+                                                 workspace.numel() if workspace is not None else 0,
+                                                 _stream_handle(stream)))
+
+
+def peer_collect(words: int, n: int, parity_stride: int, out, sync: int, stream=None) -> None:
+    """Wait for this step's n tagged words in this rank's buffer (device
+    address `words`, parity 1 `parity_stride` words further), unpack them
+    into out (fp32 device tensor of n values) and advance the step count."""
+    import torch
+    if out.numel() < n or out.dtype != torch.float32:
+        raise ValueError("out must hold n fp32 values")
+    _check(lib().hesa_cuda_peer_collect(words, n, parity_stride, out.data_ptr(), sync, _stream_handle(stream)))
 
 
 def peer_barrier(flags, rank: int, world: int, epoch: int, stream=None) -> None:

@@ -148,6 +148,56 @@ class PeerGather:
         self.base = []
 
 
+class TaggedGather:
+    """Gathered outputs as tagged 64-bit words (hesa_cuda_qmatvec_gather_tagged).
+
+    Each rank allocates two parities of `out_rows` words and its [step count,
+    ticket] pair, and maps every other rank's allocation. Matvecs of a step
+    store into every rank (targets); collect() ends the step: it waits until
+    this rank's words all carry the step's tag and unpacks them into `out`.
+    No barrier kernel, no fence: the data is its own flag.
+    """
+
+    def __init__(self, out_rows: int, rank: int, world: int, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+        import hesa_cuda as H
+        if not 1 <= world <= 8 or not 0 <= rank < world:
+            raise ValueError(f"bad rank {rank} / world {world}")
+        self.out_rows, self.rank, self.world = out_rows, rank, world
+        self.words = _align(8 * out_rows) // 8           # parity stride in words
+        self.sync_off = 2 * 8 * self.words
+        self.local, handle = H.peer_alloc(self.sync_off + 256)
+        handles = [handle]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle, group=group)
+        self.base = [self.local if p == rank else H.peer_open(handles[p]) for p in range(world)]
+        self.sync = self.local + self.sync_off
+        self.out = torch.empty(out_rows, dtype=torch.float32, device=device)
+        self.device = device
+
+    def targets(self, row0: int) -> list[int]:
+        """Addresses (parity-major, then rank) of word `row0` in every rank's buffers."""
+        return [b + par * 8 * self.words + 8 * row0 for par in (0, 1) for b in self.base]
+
+    def collect(self, stream=None):
+        """End of a step on this rank: the gathered outputs, in self.out."""
+        import hesa_cuda as H
+        H.peer_collect(self.local, self.out_rows, self.words, self.out, self.sync, stream=stream)
+        return self.out
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then free this rank's (call on every rank,
+        after a collective barrier, once no kernel uses them)."""
+        import hesa_cuda as H
+        for p, b in enumerate(self.base):
+            if p != self.rank:
+                H.peer_close(b)
+        H.peer_free(self.local)
+        self.base = []
+
+
 class GatheredQMatvec:
     """y = scale * W x with W's rows split over the ranks, the all-gather fused
     into the matvec (PeerGather). Every rank calls it with the same x and gets

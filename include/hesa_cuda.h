@@ -352,6 +352,33 @@ HESA_CUDA_API int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_r
                                            float scale, float* const* y_peers, int world, const uint32_t* epoch,
                                            void* stream);
 
+/* The same gathered matvec with every row sent as a tagged 64-bit word
+ * (value bits | tag << 32, tag = sync[0] << 12 | 1): row i goes to
+ * y_peers[b * world + p][i] for every rank p, b = sync[0] & 1, where sync
+ * (device uint32[2], zero-initialised, 8-byte aligned) is this rank's step
+ * count and collector ticket. y_peers as for hesa_cuda_qmatvec_gather, 8-byte
+ * words instead of floats. Ends with hesa_cuda_peer_collect instead of a
+ * barrier: no fence, no flags, and the launch chain stays programmatic.
+ * Shapes the row-strip kernel takes (k <= 24576) need no workspace (null,
+ * 0); longer rows run the plain matvec into `workspace` (16-byte aligned, at
+ * least hesa_cuda_gather_tagged_workspace_size bytes) and one more kernel
+ * sends its rows. */
+HESA_CUDA_API size_t hesa_cuda_gather_tagged_workspace_size(int qtype, int64_t n_rows, int64_t k);
+HESA_CUDA_API int hesa_cuda_qmatvec_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k,
+                                                  const float* x, float scale, uint64_t* const* y_peers, int world,
+                                                  const uint32_t* sync, void* workspace, size_t workspace_bytes,
+                                                  void* stream);
+
+/* End of a step of tagged gathered matvecs on this rank: waits until each of
+ * the n words of this rank's buffer for the step's parity (words while
+ * sync[0] is even, words + parity_stride while odd) carries the step's tag
+ * (each wait bounded by the peer wait limit, device status 4 on expiry),
+ * writes their values to out[0..n), then advances sync[0]. A gathered result
+ * in `out` stays valid until the next collect; the words of a parity may be
+ * overwritten from the step after next on. */
+HESA_CUDA_API int hesa_cuda_peer_collect(const uint64_t* words, int64_t n, int64_t parity_stride, float* out,
+                                         uint32_t* sync, void* stream);
+
 /* End of a step of gathered matvecs (enqueue it on the stream of those
  * matvecs: it starts after their grids have completed, which is what makes
  * their peer stores visible; it then fences at system scope): publishes

@@ -7,7 +7,9 @@ World 1 (one GPU): the sharded step's logits are bit-identical to the
 unsharded decode step's and within rel-L2 1e-5 of the oracle, for
 consecutive tokens and at the 7B widths (2 layers, vocab 32000, ctx 2048).
 World 2 (two GPUs, skipped with fewer): two processes, each holding half of
-every layer, end every step with the oracle's logits."""
+every layer, end every step with the oracle's logits, bit-identical to the
+unsharded step's (every row is summed in the same order on any number of
+ranks)."""
 import os
 import socket
 import tempfile
@@ -113,6 +115,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _cfg_for(world):
+    """The small model, with as many heads as the ranks need (8 of 64 for
+    more than two ranks)."""
+    return CFG if world <= 2 else dict(CFG, d_model=512, n_head=8, n_kv_head=8, d_ff=1024)
+
+
 def _rank_main(rank, world, port, out_dir):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -127,12 +135,12 @@ def _rank_main(rank, world, port, out_dir):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
-        c, layers, out_norm, w_out, emb = host_model(CFG)
+        c, layers, out_norm, w_out, emb = host_model(_cfg_for(world))
         full = device_full(c, layers, out_norm, w_out, dev)
         dec = sharding.ShardedDecoder(c, full, rank, world, device=dev)
         emb_d = torch.from_numpy(emb).to(dev)
         torch.cuda.synchronize(dev)
-        dist.barrier()   # the ranks meet their first peer barrier within its wait limit
+        dist.barrier()   # the ranks start their first step within the peer wait limit of one another
         for pos, tok in [(40, 5), (41, 77), (42, 383)]:
             pos_dev = torch.tensor([pos], dtype=torch.int32, device=dev)
             tok_dev = torch.tensor([tok], dtype=torch.int32, device=dev)
@@ -148,15 +156,16 @@ def _rank_main(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_two_gpus_decode_one_sequence():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gpus_decode_one_sequence(world):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     with tempfile.TemporaryDirectory() as d:
         ctx = mp.get_context("spawn")
         port = _free_port()
-        procs = [ctx.Process(target=_rank_main, args=(r, 2, port, d)) for r in range(2)]
+        procs = [ctx.Process(target=_rank_main, args=(r, world, port, d)) for r in range(world)]
         for p in procs:
             p.start()
         for p in procs:
@@ -164,13 +173,26 @@ def test_two_gpus_decode_one_sequence():
             if p.is_alive():
                 p.kill()
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-        c, layers, out_norm, w_out, emb = host_model(CFG)
+        import hesa_cuda as H
+        c, layers, out_norm, w_out, emb = host_model(_cfg_for(world))
+        ref = device_full(c, layers, out_norm, w_out, "cuda:0")
+        m = H.Model(c["n_layer"], c["d_model"], c["n_head"], c["n_kv_head"], c["head_dim"], c["d_ff"], c["vocab"],
+                    c["ctx"], c["rms_eps"], c["rope_base"], c["qtype"])
+        ws = H.decode_workspace(m)
+        lg = torch.empty(c["vocab"], dtype=torch.float32, device="cuda:0")
+        emb_d = torch.from_numpy(emb).to("cuda:0")
         for pos, tok in [(40, 5), (41, 77), (42, 383)]:
             x_ref = O.dequantize(c["qtype"], emb[tok:tok + 1], c["d_model"])[0]
             want = O.decode_step(c, layers, out_norm, w_out, x_ref, pos)
             r0 = np.load(os.path.join(d, f"r0_p{pos}.npy"))
-            r1 = np.load(os.path.join(d, f"r1_p{pos}.npy"))
-            assert np.array_equal(r0, r1), pos
+            for r in range(1, world):
+                assert np.array_equal(r0, np.load(os.path.join(d, f"r{r}_p{pos}.npy"))), (pos, r)
             assert rel_l2(r0, want) <= 1e-5, pos
-        assert int(np.load(os.path.join(d, "status0.npy"))[0]) == 0
-        assert int(np.load(os.path.join(d, "status1.npy"))[0]) == 0
+            # the unsharded step on one GPU, same token sequence
+            x = H.embed(c["qtype"], emb_d, c["d_model"], torch.tensor([tok], dtype=torch.int32, device="cuda:0"))
+            H.decode_step(m, H.make_layers(ref["layers"]), ref["out_norm"], ref["w_out"], ref["table"], x,
+                          torch.tensor([pos], dtype=torch.int32, device="cuda:0"), lg, ws)
+            torch.cuda.synchronize()
+            assert np.array_equal(r0.view(np.uint32), lg.cpu().numpy().view(np.uint32)), pos
+        for r in range(world):
+            assert int(np.load(os.path.join(d, f"status{r}.npy"))[0]) == 0, r

@@ -8,7 +8,14 @@ parities; several matvecs share one buffer at row offsets; the step replays
 from a CUDA graph with the parity following the device-side barrier count.
 Two GPUs (skipped with fewer): two processes, each holding half of W's rows,
 both end every step with the full y of the oracle. A barrier whose peer never
-arrives gives up after the configured wait and reports device status 4."""
+arrives gives up after the configured wait and reports device status 4.
+
+The tagged form (hesa_cuda_qmatvec_gather_tagged + hesa_cuda_peer_collect,
+sharding.TaggedGather): the collected rows equal the plain matvec bit for bit
+on one GPU, eagerly and from graph replays, with the step count advancing
+once per collect; a collect whose words never arrive reports status 4 after
+the configured wait; 2, 4 or 8 processes (skipped without the GPUs) each end
+every step with the oracle's full y."""
 import os
 import socket
 import tempfile
@@ -152,6 +159,88 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def test_tagged_world1_matches_plain_matvec_and_replays(torch_cuda):
+    torch = torch_cuda
+    import hesa_cuda as H
+    import sharding as S
+    # the last shape has longer rows than the strip kernel takes: plain
+    # matvec into the workspace, then the scatter kernel
+    mats = [(O.Q8_0, 300, 512), (O.Q6_K, 256, 1024), (O.Q4_K, 1000, 4096), (O.Q4_0, 77, 256), (O.Q4_K, 40, 28672)]
+    total = sum(n for _, n, _ in mats)
+    tg = S.TaggedGather(total, 0, 1, device="cuda")
+    assert H.gather_tagged_workspace(O.Q4_K, 1000, 4096) is None
+    gws = H.gather_tagged_workspace(O.Q4_K, 40, 28672)
+    assert gws is not None
+    ws, blocks, xs, tg_targets = [], [], [], []
+    off = 0
+    for i, (qt, n, k) in enumerate(mats):
+        b = O.quantize(qt, O.gaussian((n, k), 0.02, 140 + i))
+        blocks.append(b)
+        ws.append(torch.from_numpy(b).cuda())
+        xs.append(torch.from_numpy(O.gaussian((k,), 1.0, 150 + i)).cuda())
+        tg_targets.append(tg.targets(off))
+        off += n
+    stream = torch.cuda.Stream()
+
+    def step():
+        for (qt, n, k), w, x, t in zip(mats, ws, xs, tg_targets):
+            H.qmatvec_gather_tagged(qt, w, x, t, 1, tg.sync, scale=0.25, workspace=gws if k > 24576 else None,
+                                    stream=stream)
+        tg.collect(stream=stream)
+
+    want = np.concatenate([O.qmatvec(qt, b, x.cpu().numpy(), scale=0.25) for (qt, n, k), b, x in
+                           zip(mats, blocks, xs)])
+    plain = torch.cat([H.qmatvec(qt, w, x, scale=0.25) for (qt, n, k), w, x in zip(mats, ws, xs)])
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+        stream.synchronize()
+        assert torch.equal(tg.out, plain)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        tg.out.zero_()
+        for _ in range(5):
+            graph.replay()
+    stream.synchronize()
+    assert int(H.device_view(tg.sync, 1, dtype="<i4")[0]) == 8   # 3 eager + 5 replays
+    assert int(H.device_view(tg.sync + 4, 1, dtype="<i4")[0]) == 0
+    assert torch.equal(tg.out, plain)
+    assert rel_l2(tg.out.cpu().numpy(), want) <= REL_L2_TOL
+    del graph
+    assert H.device_status() == 0
+    tg.close()
+
+
+def test_tagged_collect_wait_runs_out_and_reports_status_4(torch_cuda):
+    torch = torch_cuda
+    import time
+    import hesa_cuda as H
+    import sharding as S
+    tg = S.TaggedGather(1000, 0, 1, device="cuda")
+    H.set_peer_wait_limit(0.05)
+    try:
+        t0 = time.time()
+        tg.collect()            # nothing stored this step's words: every wait runs out once
+        st = H.device_status()
+        assert st == 4, st
+        assert time.time() - t0 < 10
+    finally:
+        H.set_peer_wait_limit(0)
+        H.clear_device_status()
+    # the context stays usable: a real step afterwards (count 1, parity 1)
+    qt, n, k = O.Q4_K, 1000, 1024
+    b = O.quantize(qt, O.gaussian((n, k), 0.02, 160))
+    x = O.gaussian((k,), 1.0, 161)
+    w = torch.from_numpy(b).cuda()
+    H.qmatvec_gather_tagged(qt, w, torch.from_numpy(x).cuda(), tg.targets(0), 1, tg.sync)
+    y = tg.collect()
+    torch.cuda.synchronize()
+    assert rel_l2(y.cpu().numpy(), O.qmatvec(qt, b, x)) <= REL_L2_TOL
+    assert H.device_status() == 0
+    tg.close()
+
+
 def _rank_main(rank, world, port, out_dir):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -185,6 +274,72 @@ def _rank_main(rank, world, port, out_dir):
         with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
             f.write(status)
         dist.destroy_process_group()
+
+
+def _tagged_rank_main(rank, world, port, out_dir):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "hesa-llm_b200")]
+    from datetime import timedelta
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    status = "fail"
+    try:
+        from oracle import oracle as Orc
+        import hesa_cuda as H
+        import sharding as S
+        mats = [(Orc.Q4_K, 4100, 4096), (Orc.Q6_K, 515, 1024)]
+        total = sum(n for _, n, _ in mats)
+        tg = S.TaggedGather(total, rank, world, device="cuda")
+        shards = []
+        off = 0
+        for i, (qt, n, k) in enumerate(mats):
+            blocks = Orc.quantize(qt, Orc.gaussian((n, k), 0.02, 170 + i))
+            r0, r1 = S.row_range(n, rank, world)
+            shards.append((qt, n, k, blocks, torch.from_numpy(blocks[r0:r1]).cuda(), tg.targets(off + r0)))
+            off += n
+        dist.barrier()
+        errs = []
+        for step in range(4):    # both parities twice, ranks not in lockstep between steps
+            xs = [Orc.gaussian((k,), 1.0, 180 + 10 * step + i) for i, (_, _, k) in enumerate(mats)]
+            for (qt, n, k, blocks, w, t), x in zip(shards, xs):
+                H.qmatvec_gather_tagged(qt, w, torch.from_numpy(x).cuda(), t, world, tg.sync)
+            y = tg.collect().cpu().numpy()
+            want = np.concatenate([Orc.qmatvec(qt, blocks, x) for (qt, n, k, blocks, w, t), x in zip(shards, xs)])
+            errs.append(rel_l2(y, want))
+        ok = max(errs) <= REL_L2_TOL and H.device_status() == 0
+        torch.cuda.synchronize()
+        dist.barrier()
+        tg.close()
+        status = "ok" if ok else f"errors {errs}"
+    finally:
+        with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+            f.write(status)
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gpus_tagged_gather_the_full_output(torch_cuda, world):
+    torch = torch_cuda
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.get_context("spawn")
+        port = _free_port()
+        procs = [ctx.Process(target=_tagged_rank_main, args=(r, world, port, d)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            if p.is_alive():
+                p.kill()
+                pytest.fail("rank did not finish")
+        for r in range(world):
+            assert open(os.path.join(d, f"r{r}.txt")).read() == "ok", r
 
 
 def test_two_gpus_gather_the_full_output(torch_cuda):
