@@ -504,17 +504,16 @@ def run_proj70b(dev, stream, rank: int, world: int, pg=None, reps: int = 20):
         # the gather's workspace: only the down projection (k = 28672, longer
         # rows than the strip kernel takes) needs one
         gws = H.gather_tagged_workspace(qt, r1 - r0, k, device=dev) if tg else None
-        mats.append((w, x, y, H.make_workspace(qt, r1 - r0, k, device=dev), tg.targets(off + r0) if tg else None,
-                     gws))
+        mats.append((w, x, y, H.make_workspace(qt, r1 - r0, k, device=dev), off + r0, gws))
         off += n
 
     def local():
-        for w, x, y, ws, t, gws in mats:
+        for w, x, y, ws, row0, gws in mats:
             H.qmatvec(qt, w, x, y=y, workspace=ws, stream=stream)
 
     def gathered():
-        for w, x, y, ws, t, gws in mats:
-            H.qmatvec_gather_tagged(qt, w, x, t, world, tg.sync, workspace=gws, stream=stream)
+        for w, x, y, ws, row0, gws in mats:
+            H.qmatvec_gather_tagged(qt, w, x, tg.targets(), row0, world, tg.sync, workspace=gws, stream=stream)
         tg.collect(stream=stream)
 
     def timed(body):
@@ -709,7 +708,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         peers = sharding.TaggedGather(y_all.numel(), rank, world, device=dev)
         off = rank * y_local.numel()
         for name, qt, n, k, wt, xt, yt, ws in dmats:
-            targets.append(peers.targets(off))
+            targets.append(off)
             off += n
         pg.barrier()
 
@@ -730,8 +729,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     def one_step():
         if peers is None:
             return one_step_nccl()
-        for (name, qt, n, k, wt, xt, yt, ws), tgt in zip(dmats, targets):
-            H.qmatvec_gather_tagged(qt, wt, xt, tgt, world, peers.sync, stream=stream)
+        for (name, qt, n, k, wt, xt, yt, ws), row0 in zip(dmats, targets):
+            H.qmatvec_gather_tagged(qt, wt, xt, peers.targets(), row0, world, peers.sync, stream=stream)
         peers.collect(stream=stream)
 
     if args.profile:

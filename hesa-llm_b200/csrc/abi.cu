@@ -204,10 +204,11 @@ size_t hesa_cuda_gather_tagged_workspace_size(int qtype, int64_t n_rows, int64_t
 }
 
 int hesa_cuda_qmatvec_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x,
-                                    float scale, uint64_t* const* y_peers, int world, const uint32_t* sync,
-                                    void* workspace, size_t workspace_bytes, void* stream) {
+                                    float scale, uint64_t* const* y_peers, int64_t row0, int world,
+                                    const uint32_t* sync, void* workspace, size_t workspace_bytes, void* stream) {
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w || !x || !y_peers || !sync) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
+    if (row0 < 0 || row0 >= (int64_t(1) << 40)) return fail(HESA_CUDA_INVALID_ARGUMENT, "bad row offset");
     if (world < 1 || world > hesa_cuda::kMaxPeers) return fail(HESA_CUDA_INVALID_ARGUMENT, "world must be 1..8");
     if (n_rows <= 0 || k <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "non-positive dimension");
     if (n_rows >= (int64_t(1) << 30) || k % 256 != 0)
@@ -223,9 +224,11 @@ int hesa_cuda_qmatvec_gather_tagged(int qtype, const void* w, int64_t n_rows, in
         for (int p = 0; p < world; ++p) {
             uint64_t* q = y_peers[b * world + p];
             if (!q) return fail(HESA_CUDA_INVALID_ARGUMENT, "null output pointer");
-            if (reinterpret_cast<uintptr_t>(q) & 7) return fail(HESA_CUDA_INVALID_ARGUMENT, "outputs must be 8-byte aligned");
+            if (reinterpret_cast<uintptr_t>(q) & 15)
+                return fail(HESA_CUDA_INVALID_ARGUMENT, "gathered buffers must be 16-byte aligned");
             (b == 0 ? out.y : out.y2)[p] = q;
         }
+    out.off = row0;
     out.world = world;
     out.by_parity = 1;
     out.count = sync;
@@ -249,9 +252,10 @@ int hesa_cuda_peer_collect(const uint64_t* words, int64_t n, int64_t parity_stri
                            void* stream) {
     if (!words || !out || !sync) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n <= 0 || n >= (int64_t(1) << 30)) return fail(HESA_CUDA_SHAPE_MISMATCH, "word count must be 1 .. 2^30 - 1");
-    if (parity_stride < n) return fail(HESA_CUDA_SHAPE_MISMATCH, "the two parities overlap");
-    if ((reinterpret_cast<uintptr_t>(words) & 7) || (reinterpret_cast<uintptr_t>(sync) & 7))
-        return fail(HESA_CUDA_INVALID_ARGUMENT, "words and sync must be 8-byte aligned");
+    if (parity_stride < ((n + 255) & ~int64_t(255)) || parity_stride % 256 != 0)
+        return fail(HESA_CUDA_SHAPE_MISMATCH, "each parity holds whole units of 256 words");
+    if ((reinterpret_cast<uintptr_t>(words) & 15) || (reinterpret_cast<uintptr_t>(sync) & 7))
+        return fail(HESA_CUDA_INVALID_ARGUMENT, "words must be 16-byte and sync 8-byte aligned");
     const cudaError_t e = hesa_cuda::peer_collect(words, words + parity_stride, n, out, sync, kGatherTagLo,
                                                   static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? HESA_CUDA_OK : cuda_fail(e, "peer collect kernel");

@@ -286,10 +286,11 @@ struct AttnRope {
     const float* table;   // rope table [table_rows][head_dim]: cos, then sin
     int table_rows;
     int* status;
-    // head-sharded decode: head h's output goes to peer_out[p] + h * head_dim
-    // on every rank p (this rank's first head's place in rank p's buffer) as
-    // tagged words (peer_sync.cuh); peer_world 0: to out
+    // head-sharded decode: element h * head_dim + d of this rank's heads goes
+    // to element peer_off + h * head_dim + d of the tagged vector at
+    // peer_out[p] on every rank p (peer_sync.cuh); peer_world 0: to out
     uint64_t* peer_out[kPeerSyncMax];
+    int64_t peer_off;
     int peer_world;
     const uint32_t* ll_count;
     uint32_t ll_lo;
@@ -580,7 +581,8 @@ attention_kernel(const float* __restrict__ q, const __half* __restrict__ kc, con
                     out[o] = a * inv;
                 } else {
                     const uint32_t tag = ll_tag(ri.ll_count, ri.ll_lo);
-                    for (int p = 0; p < ri.peer_world; ++p) st_ll(ri.peer_out[p] + o, a * inv, tag);
+                    const int64_t at = ll_pos(ri.peer_off + o);
+                    for (int p = 0; p < ri.peer_world; ++p) st_ll(ri.peer_out[p] + at, a * inv, tag);
                 }
             }
             if (lane == 0) {
@@ -759,14 +761,14 @@ cudaError_t attention_rope(const float* q, const float* k_new, const float* v_ne
                            int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
                            cudaStream_t s) {
     return attention_rope_shard(q, k_new, v_new, kc, vc, out, n_head, n_kv_head, head_dim, table, table_rows, ctx,
-                                pos_dev, workspace, nullptr, 0, nullptr, 0u, s);
+                                pos_dev, workspace, nullptr, 0, 0, nullptr, 0u, s);
 }
 
 cudaError_t attention_rope_shard(const float* q, const float* k_new, const float* v_new, void* kc, void* vc,
                                  float* out, int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
                                  int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
-                                 uint64_t* const* peer_out, int peer_world, const uint32_t* ll_count, uint32_t ll_lo,
-                                 cudaStream_t s) {
+                                 uint64_t* const* peer_out, int64_t peer_off, int peer_world, const uint32_t* ll_count,
+                                 uint32_t ll_lo, cudaStream_t s) {
     int* status = nullptr;
     cudaError_t e = status_word(&status);
     if (e != cudaSuccess) return e;
@@ -781,6 +783,7 @@ cudaError_t attention_rope_shard(const float* q, const float* k_new, const float
     ri.table_rows = table_rows;
     ri.status = status;
     ri.peer_world = peer_world;
+    ri.peer_off = peer_off;
     for (int p = 0; p < peer_world; ++p) {
         if (!peer_out[p]) return cudaErrorInvalidValue;
         ri.peer_out[p] = peer_out[p];

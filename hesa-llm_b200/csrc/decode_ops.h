@@ -38,13 +38,14 @@ cudaError_t attention_rope(const float* q, const float* k_new, const float* v_ne
                            int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
                            int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
                            cudaStream_t s);
-// attention_rope of this rank's heads in a head-sharded decode step: head h's
-// output goes to peer_out[p] + h * head_dim of every rank p as tagged words
-// (tag (*ll_count << 12) | ll_lo, peer_sync.cuh).
+// attention_rope of this rank's heads in a head-sharded decode step: element
+// h * head_dim + d of its output is element peer_off + h * head_dim + d of the
+// tagged vector at peer_out[p] on every rank p (tag (*ll_count << 12) | ll_lo;
+// element order as peer_sync.cuh).
 cudaError_t attention_rope_shard(const float* q, const float* k_new, const float* v_new, void* kc, void* vc,
                                  float* out, int64_t n_head, int64_t n_kv_head, int64_t head_dim, const float* table,
                                  int32_t table_rows, int64_t ctx, const int32_t* pos_dev, void* workspace,
-                                 uint64_t* const* peer_out, int peer_world, const uint32_t* ll_count, uint32_t ll_lo,
-                                 cudaStream_t s);
+                                 uint64_t* const* peer_out, int64_t peer_off, int peer_world,
+                                 const uint32_t* ll_count, uint32_t ll_lo, cudaStream_t s);
 
 }  // namespace hesa_cuda

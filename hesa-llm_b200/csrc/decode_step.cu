@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(1024) ll_fill_kernel(const float* __restrict__
                                                        uint32_t* count) {
     const uint32_t c = *reinterpret_cast<volatile uint32_t*>(count) + 1u;
     const uint32_t tag = (c << 12) | lo_of(0, kPhEmbed);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) st_ll(x_ll + i, x[i], tag);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) st_ll(x_ll + ll_pos(i), x[i], tag);
     __syncthreads();
     if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(count) = c;
 }
@@ -284,9 +284,16 @@ __global__ void __launch_bounds__(1024) ll_fill_kernel(const float* __restrict__
 __global__ void ll_unpack_kernel(const uint64_t* ll, float* __restrict__ out, int n, const uint32_t* count,
                                  uint32_t lo, unsigned long long limit_ns, int* status) {
     const uint32_t tag = ll_tag(count, lo);
-    bool ok = true;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
-        out[i] = ld_ll_wait(ll + i, tag, limit_ns, status, ok);
+    __shared__ int failed;
+    if (threadIdx.x == 0) failed = 0;
+    __syncthreads();
+    // words in order (coalesced), each to its element (the tail of the last
+    // unit holds none)
+    const int n_words = (n + 255) & ~255;
+    for (int w = blockIdx.x * blockDim.x + threadIdx.x; w < n_words; w += gridDim.x * blockDim.x) {
+        const int e = static_cast<int>(ll_elem(w));
+        if (e < n) out[e] = ld_ll_wait(ll + w, tag, limit_ns, status, &failed);
+    }
 }
 
 }  // namespace
@@ -305,9 +312,13 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
     if (W < 1 || W > kPeerSyncMax || r < 0 || r >= W) return record_error(HESA_CUDA_INVALID_ARGUMENT, "bad rank / world");
     if (!sh->x_peers || !sh->a_peers || !sh->gu_peers || !sh->logits_peers || !sh->token_count)
         return record_error(HESA_CUDA_INVALID_ARGUMENT, "null shard buffer array");
-    for (int p = 0; p < W; ++p)
+    for (int p = 0; p < W; ++p) {
         if (!sh->x_peers[p] || !sh->a_peers[p] || !sh->gu_peers[p] || !sh->logits_peers[p])
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "null peer buffer");
+        if ((reinterpret_cast<uintptr_t>(sh->x_peers[p]) | reinterpret_cast<uintptr_t>(sh->a_peers[p]) |
+             reinterpret_cast<uintptr_t>(sh->gu_peers[p]) | reinterpret_cast<uintptr_t>(sh->logits_peers[p])) & 15)
+            return record_error(HESA_CUDA_INVALID_ARGUMENT, "peer buffers must be 16-byte aligned");
+    }
     if (m->n_head % W != 0 || m->n_kv_head % W != 0)
         return record_error(HESA_CUDA_SHAPE_MISMATCH, "n_head and n_kv_head must be multiples of world");
     if (m->n_layer >= 512) return record_error(HESA_CUDA_SHAPE_MISMATCH, "n_layer must be below 512");
@@ -357,25 +368,30 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
     const unsigned long long limit_ns = peer_wait_limit();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-    auto in = [&](const uint64_t* x, uint32_t x_lo, const uint64_t* resid, uint32_t resid_lo) {
+    // vectors by their word 0; the residual's rows of this shard start at
+    // element resid_off
+    auto in = [&](const uint64_t* x, uint32_t x_lo, const uint64_t* resid, int64_t resid_off, uint32_t resid_lo) {
         LLIn li = {};
         li.x = x;
         li.resid = resid;
+        li.resid_off = resid_off;
         li.count = cnt;
         li.x_lo = x_lo;
         li.resid_lo = resid_lo;
         li.limit_ns = limit_ns;
         return li;
     };
-    // this rank's part lands at `off` of every rank's buffer (rows from
-    // `split` on at off2 of bufs2)
+    // this rank's rows are elements off.. of every rank's vector (rows from
+    // `split` on: elements off2.. of bufs2)
     auto out = [&](uint64_t* const* bufs, int64_t off, int64_t n_rows, uint64_t* const* bufs2, int64_t off2,
                    int64_t split, uint32_t lo) {
         LLOut o = {};
         for (int p = 0; p < W; ++p) {
-            o.y[p] = bufs[p] + off;
-            o.y2[p] = bufs2 ? bufs2[p] + off2 : nullptr;
+            o.y[p] = bufs[p];
+            o.y2[p] = bufs2 ? bufs2[p] : nullptr;
         }
+        o.off = off;
+        o.off2 = off2;
         o.split = static_cast<int>(bufs2 ? split : n_rows);
         o.world = W;
         o.count = cnt;
@@ -392,7 +408,7 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
     e = cudaGetLastError();
     if (e != cudaSuccess) return record_cuda_error(e, "embedding fill");
     uint64_t* a_out[kPeerSyncMax] = {};
-    for (int p = 0; p < W; ++p) a_out[p] = sh->a_peers[p] + r * qd_r;
+    for (int p = 0; p < W; ++p) a_out[p] = sh->a_peers[p];
     int rc = HESA_CUDA_OK;
     for (int l = 0; l < m->n_layer && rc == HESA_CUDA_OK; ++l) {
         const hesa_cuda_layer& Ly = layers[l];
@@ -408,32 +424,32 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
         // the residual as the previous exchange left it
         const uint32_t x_lo = l == 0 ? lo_of(0, kPhEmbed) : lo_of(l - 1, kPhDown);
         // q|k|v of this rank's heads (local)
-        rc = strip(Ly.wq, qd_r + 2 * kd_r, D, SI::kRmsNorm, Ly.attn_norm, q, in(x_own, x_lo, nullptr, 0), LLOut{},
+        rc = strip(Ly.wq, qd_r + 2 * kd_r, D, SI::kRmsNorm, Ly.attn_norm, q, in(x_own, x_lo, nullptr, 0, 0), LLOut{},
                    "sharded q|k|v");
         if (rc) break;
         // attention of this rank's heads -> every rank's a
         e = attention_rope_shard(q, k, v, Ly.k_cache, Ly.v_cache, nullptr, hl, kvl, HD, rope_table, rope_rows, m->ctx,
-                                 pos_dev, att_ws, a_out, W, cnt, lo_of(l, kPhAttn), s);
+                                 pos_dev, att_ws, a_out, r * qd_r, W, cnt, lo_of(l, kPhAttn), s);
         if (e != cudaSuccess) return record_cuda_error(e, "sharded attention");
         // x[d0:d1] += Wo a -> every rank's x
         rc = strip(Ly.wo, d1 - d0, QD, SI::kPlain, nullptr, nullptr,
-                   in(sh->a_peers[r], lo_of(l, kPhAttn), x_own + d0, x_lo),
+                   in(sh->a_peers[r], lo_of(l, kPhAttn), x_own, d0, x_lo),
                    out(sh->x_peers, d0, d1 - d0, nullptr, 0, 0, lo_of(l, kPhWo)), "sharded Wo");
         // gate|up rows of this rank -> every rank's gate|up
         if (!rc)
             rc = strip(Ly.w_gate, 2 * (f1 - f0), D, SI::kRmsNorm, Ly.ffn_norm, nullptr,
-                       in(x_own, lo_of(l, kPhWo), nullptr, 0),
+                       in(x_own, lo_of(l, kPhWo), nullptr, 0, 0),
                        out(sh->gu_peers, f0, 2 * (f1 - f0), sh->gu_peers, F + f0, f1 - f0, lo_of(l, kPhGateUp)),
                        "sharded gate|up");
         // x[d0:d1] += Wdown silu(g) u -> every rank's x
         if (!rc)
             rc = strip(Ly.w_down, d1 - d0, F, SI::kSiluMul, nullptr, nullptr,
-                       in(sh->gu_peers[r], lo_of(l, kPhGateUp), x_own + d0, lo_of(l, kPhWo)),
+                       in(sh->gu_peers[r], lo_of(l, kPhGateUp), x_own, d0, lo_of(l, kPhWo)),
                        out(sh->x_peers, d0, d1 - d0, nullptr, 0, 0, lo_of(l, kPhDown)), "sharded W_down");
     }
     const int64_t NL = m->n_layer;
     if (!rc)
-        rc = strip(w_out, v1 - v0, D, SI::kRmsNorm, out_norm, nullptr, in(x_own, lo_of(NL - 1, kPhDown), nullptr, 0),
+        rc = strip(w_out, v1 - v0, D, SI::kRmsNorm, out_norm, nullptr, in(x_own, lo_of(NL - 1, kPhDown), nullptr, 0, 0),
                    out(sh->logits_peers, v0, v1 - v0, nullptr, 0, 0, lo_of(NL, kPhLogits)), "sharded LM head");
     if (!rc) {
         const int grid = static_cast<int>(std::min<int64_t>((V + 255) / 256, 148));

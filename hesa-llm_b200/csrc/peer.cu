@@ -86,9 +86,16 @@ __global__ void __launch_bounds__(kCollectThreads) peer_collect_kernel(const uin
     const uint32_t c = *reinterpret_cast<volatile uint32_t*>(sync);
     const uint32_t tag = (c << 12) | lo;
     const uint64_t* src = (c & 1u) ? words1 : words0;
-    bool ok = true;
-    for (int i = blockIdx.x * kCollectThreads + threadIdx.x; i < n; i += gridDim.x * kCollectThreads)
-        out[i] = ld_ll_wait(src + i, tag, limit_ns, status, ok);
+    __shared__ int failed;
+    if (threadIdx.x == 0) failed = 0;
+    __syncthreads();
+    // words in order (coalesced), each to its element; the words of the last
+    // unit past n hold no element
+    const int n_words = (n + 255) & ~255;
+    for (int w = blockIdx.x * kCollectThreads + threadIdx.x; w < n_words; w += gridDim.x * kCollectThreads) {
+        const int e = static_cast<int>(ll_elem(w));
+        if (e < n) out[e] = ld_ll_wait(src + w, tag, limit_ns, status, &failed);
+    }
     // the last CTA to finish advances the count (every CTA has read it by then)
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -109,7 +116,8 @@ __global__ void __launch_bounds__(kCollectThreads) peer_scatter_kernel(const flo
     const bool odd = (tag >> 12) & 1u;
     for (int i = blockIdx.x * kCollectThreads + threadIdx.x; i < n; i += gridDim.x * kCollectThreads) {
         const float v = y[i];
-        for (int p = 0; p < o.world; ++p) st_ll((odd ? o.y2[p] : o.y[p]) + i, v, tag);
+        const int64_t at = ll_pos(o.off + i);
+        for (int p = 0; p < o.world; ++p) st_ll((odd ? o.y2[p] : o.y[p]) + at, v, tag);
     }
 }
 

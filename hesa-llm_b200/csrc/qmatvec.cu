@@ -400,12 +400,16 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     int* issued = done + kStripMaxSlots;
     float* red = reinterpret_cast<float*>(issued + kStripMaxSlots);   // kWarps floats
 
+    // set once a wait for a tagged input of this CTA ran out (later waits
+    // then take what they read)
+    __shared__ int s_ll_failed;
     if (threadIdx.x == 0) {
         for (int s = 0; s < n_slots; ++s) {
             mbar_init(&full[s], 1);
             done[s] = 0;
             issued[s] = -1;
         }
+        s_ll_failed = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -443,9 +447,21 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     // per token on two GPUs (its polling competes with the producer)
     grid_dep_wait();
     // tagged inputs (sharded decode step): the tags of this token
-    bool ll_ok = true;
-    uint32_t x_tag = 0;
-    if constexpr (LLX) x_tag = ll_tag(lin.count, lin.x_lo);
+    // (the counts are read here, not where the tags are needed, so that the
+    // epilogue does not start with a round trip to L2)
+    uint32_t x_tag = 0, rtag = 0, out_tag = 0;
+    if constexpr (LLX) {
+        x_tag = ll_tag(lin.count, lin.x_lo);
+        rtag = (x_tag & ~0xFFFu) | lin.resid_lo;
+    }
+    if constexpr (OUT == kOutTagged) out_tag = ll_tag(lout.count, lout.lo);
+    // the residual word of this thread's first row, read now (it arrived with
+    // the input of an earlier kernel) and checked in the epilogue
+    uint64_t resid_w = 0;
+    if constexpr (LLX && OUT == kOutTagged) {
+        if (lin.resid && static_cast<int>(threadIdx.x) < nrows)
+            resid_w = ld_ll(lin.resid + ll_pos(lin.resid_off + r0 + static_cast<int>(threadIdx.x)));
+    }
 
     // x as digit planes, converted once per CTA (one warp per unit of 256;
     // the loads of a batch of units are issued together). The input may be
@@ -456,7 +472,7 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         float v[kStripBatch][8];
         float ss = 0.f;
         if constexpr (LLX) {
-            load8_ll_batch(lin.x, x_tag, lin.limit_ns, warp, lane, U, v, status, ll_ok);
+            load8_ll_batch(lin.x, x_tag, lin.limit_ns, warp, lane, U, v, status, &s_ll_failed);
 #pragma unroll
             for (int jb = 0; jb < kStripBatch; ++jb)
 #pragma unroll
@@ -491,15 +507,10 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         for (int ub = warp; ub < U; ub += kWarps * kStripBatch) {
             float v[kStripBatch][8];
             if constexpr (LLX) {
-                load8_ll_batch(lin.x, x_tag, lin.limit_ns, ub, lane, U, v, status, ll_ok);
-                if (xmode == kXSiluMul) {
-                    float up[kStripBatch][8];
-                    load8_ll_batch(lin.x + k, x_tag, lin.limit_ns, ub, lane, U, up, status, ll_ok);
-#pragma unroll
-                    for (int jb = 0; jb < kStripBatch; ++jb)
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) v[jb][j] = swiglu_x(v[jb][j], up[jb][j]);
-                }
+                if (xmode == kXSiluMul)
+                    load8_ll_swiglu(lin.x, k, x_tag, lin.limit_ns, ub, lane, U, v, status, &s_ll_failed);
+                else
+                    load8_ll_batch(lin.x, x_tag, lin.limit_ns, ub, lane, U, v, status, &s_ll_failed);
             } else {
 #pragma unroll
                 for (int jb = 0; jb < kStripBatch; ++jb) {
@@ -602,9 +613,7 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
     if constexpr (OUT == kOutTagged) {
         // every row to every rank, tagged with this step's place (sharded
         // decode step, tagged gather)
-        const uint32_t tag = ll_tag(lout.count, lout.lo);
-        uint32_t rtag = 0;
-        if constexpr (LLX) rtag = lin.resid ? ll_tag(lin.count, lin.resid_lo) : 0u;
+        const uint32_t tag = out_tag;
         const bool odd = lout.by_parity && ((tag >> 12) & 1u);
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
             float s = 0.f;
@@ -612,13 +621,18 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
             const int row = r0 + i;
             float val = s * scale;
             if constexpr (LLX) {
-                if (lin.resid) val = __fadd_rn(ld_ll_wait(lin.resid + row, rtag, lin.limit_ns, status, ll_ok), val);
+                if (lin.resid) {
+                    const uint64_t* ra = lin.resid + ll_pos(lin.resid_off + row);
+                    const float rv = i == static_cast<int>(threadIdx.x)
+                                         ? ll_value(ra, resid_w, rtag, lin.limit_ns, status, &s_ll_failed)
+                                         : ld_ll_wait(ra, rtag, lin.limit_ns, status, &s_ll_failed);
+                    val = __fadd_rn(rv, val);
+                }
             }
-            for (int p = 0; p < lout.world; ++p) {
-                if (lout.by_parity) st_ll((odd ? lout.y2[p] : lout.y[p]) + row, val, tag);
-                else if (row < lout.split) st_ll(lout.y[p] + row, val, tag);
-                else st_ll(lout.y2[p] + (row - lout.split), val, tag);
-            }
+            const bool second = !lout.by_parity && row >= lout.split;
+            const int64_t at = second ? ll_pos(lout.off2 + (row - lout.split)) : ll_pos(lout.off + row);
+            for (int p = 0; p < lout.world; ++p)
+                st_ll(((lout.by_parity ? odd : second) ? lout.y2[p] : lout.y[p]) + at, val, tag);
         }
     } else if constexpr (OUT == kOutPlain) {
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {

@@ -73,8 +73,9 @@ cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k,
                             cudaStream_t stream);
 
 // Row-sharded matvec whose rows reach every rank as tagged words: row i to
-// lout.y[p] + i (lout.y2[p] + i while the count is odd; lout.by_parity must be
-// set) with the tag (*lout.count << 12) | lout.lo. x is a plain local vector.
+// element lout.off + i of lout.y[p] (of lout.y2[p] while the count is odd;
+// lout.by_parity must be set; element order as peer_sync.cuh) with the tag
+// (*lout.count << 12) | lout.lo. x is a plain local vector.
 cudaError_t qmv_strip_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
                                     const LLOut& lout, cudaStream_t stream);
 
@@ -84,10 +85,10 @@ cudaError_t qmv_strip_gather_tagged(int qtype, const void* w, int64_t n_rows, in
 cudaError_t peer_scatter_tagged(const float* y, int64_t n, const LLOut& lout, cudaStream_t stream);
 
 // End of a step of tagged gathers on this rank: waits (bounded by the peer
-// wait limit; kStatusPeerTimeout on expiry) until each of the n words of this
-// rank's buffer of the step's parity (words0 while sync[0] is even, words1
-// while odd) carries the tag (sync[0] << 12) | lo, writes their values to
-// out, then advances sync[0]. sync[1] is the launch's CTA ticket (zero between
+// wait limit; kStatusPeerTimeout on expiry) until each of the n elements of
+// this rank's buffer of the step's parity (words0 while sync[0] is even,
+// words1 while odd; whole units of 256 words) carries the tag
+// (sync[0] << 12) | lo, writes their values to out, then advances sync[0]. sync[1] is the launch's CTA ticket (zero between
 // launches). Launched with programmatic serialization; it waits for the grids
 // before it.
 cudaError_t peer_collect(const uint64_t* words0, const uint64_t* words1, int64_t n, float* out, uint32_t* sync,

@@ -343,20 +343,56 @@ __device__ __forceinline__ float swiglu_x(float g, float u) { return __fdividef(
 // `tag`, for the kStripBatch units u0 + jb * kWarps: the loads of two units
 // are issued before the first of their tags is looked at (more would spill).
 __device__ __forceinline__ void load8_ll_batch(const uint64_t* src, uint32_t tag, unsigned long long limit_ns, int u0,
-                                               int lane, int U, float (&v)[kStripBatch][8], int* status, bool& ok) {
+                                               int lane, int U, float (&v)[kStripBatch][8], int* status,
+                                               volatile int* failed) {
 #pragma unroll
     for (int jh = 0; jh < kStripBatch; jh += 2) {
         uint64_t w[2][8];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
             const int u = u0 + (jh + i) * kWarps;
-            if (u < U) ld_ll8_issue(src + static_cast<size_t>(u) * 256 + lane * 8, w[i]);
+            if (u < U) ld_ll8_issue(src + static_cast<size_t>(u) * 256, lane, w[i]);
         }
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
             const int u = u0 + (jh + i) * kWarps;
             if (u < U) {
-                ld_ll8_take(src + static_cast<size_t>(u) * 256 + lane * 8, w[i], tag, limit_ns, v[jh + i], status, ok);
+                ld_ll8_take(src + static_cast<size_t>(u) * 256, lane, w[i], tag, limit_ns, v[jh + i], status,
+                            failed);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[jh + i][j] = 0.f;
+            }
+        }
+    }
+}
+
+// SwiGLU input from a tagged vector (gate at src, up at src + k elements):
+// v[jb] <- swiglu_x(gate, up) for the units u0 + jb * kWarps, the loads of
+// both halves of two units issued before the first tag is looked at.
+__device__ __forceinline__ void load8_ll_swiglu(const uint64_t* src, int64_t k, uint32_t tag,
+                                                unsigned long long limit_ns, int u0, int lane, int U,
+                                                float (&v)[kStripBatch][8], int* status, volatile int* failed) {
+#pragma unroll
+    for (int jh = 0; jh < kStripBatch; jh += 2) {
+        uint64_t wg[2][8], wu[2][8];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int u = u0 + (jh + i) * kWarps;
+            if (u < U) {
+                ld_ll8_issue(src + static_cast<size_t>(u) * 256, lane, wg[i]);
+                ld_ll8_issue(src + k + static_cast<size_t>(u) * 256, lane, wu[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int u = u0 + (jh + i) * kWarps;
+            if (u < U) {
+                float g[8], up[8];
+                ld_ll8_take(src + static_cast<size_t>(u) * 256, lane, wg[i], tag, limit_ns, g, status, failed);
+                ld_ll8_take(src + k + static_cast<size_t>(u) * 256, lane, wu[i], tag, limit_ns, up, status, failed);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[jh + i][j] = swiglu_x(g[j], up[j]);
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) v[jh + i][j] = 0.f;

@@ -76,8 +76,8 @@ SIGNATURES = [
     ("hesa_cuda_qmatvec_gather", _int, [_int, _vp, _i64, _i64, _vp, _f, ctypes.POINTER(_vp), _int, _vp, _vp]),
     ("hesa_cuda_peer_barrier", _int, [ctypes.POINTER(_vp), _int, _int, _vp, _vp]),
     ("hesa_cuda_gather_tagged_workspace_size", _sz, [_int, _i64, _i64]),
-    ("hesa_cuda_qmatvec_gather_tagged", _int, [_int, _vp, _i64, _i64, _vp, _f, ctypes.POINTER(_vp), _int, _vp, _vp,
-                                               _sz, _vp]),
+    ("hesa_cuda_qmatvec_gather_tagged", _int, [_int, _vp, _i64, _i64, _vp, _f, ctypes.POINTER(_vp), _i64, _int,
+                                               _vp, _vp, _sz, _vp]),
     ("hesa_cuda_peer_collect", _int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     ("hesa_cuda_set_peer_wait_limit_us", _int, [ctypes.c_uint32]),
     ("hesa_cuda_decode_step_sharded", _int, [ctypes.POINTER(Model), _vp, ctypes.POINTER(Layer), _vp, _vp, _vp,
@@ -247,27 +247,30 @@ def gather_tagged_workspace(qtype: int, n_rows: int, k: int, device=None):
     return torch.zeros(nbytes, dtype=torch.uint8, device=device or "cuda") if nbytes else None
 
 
-def qmatvec_gather_tagged(qtype: int, w, x, y_peers, world: int, sync: int, scale: float = 1.0, workspace=None,
-                          stream=None):
-    """As qmatvec_gather, every row stored as a tagged 64-bit word; y_peers
-    lists 2 * world device addresses (parity-major) of this shard's first word
-    in each rank's buffers; sync is the device address of this rank's
-    [step count, ticket] pair. The step ends with peer_collect. Rows longer
-    than the strip kernel takes need `workspace` (gather_tagged_workspace)."""
+def qmatvec_gather_tagged(qtype: int, w, x, y_peers, row0: int, world: int, sync: int, scale: float = 1.0,
+                          workspace=None, stream=None):
+    """As qmatvec_gather, every row stored as a tagged 64-bit word: row i is
+    element row0 + i of the gathered vector; y_peers lists 2 * world device
+    addresses (parity-major) of word 0 of each rank's gathered buffers; sync
+    is the device address of this rank's [step count, ticket] pair. The step
+    ends with peer_collect. Rows longer than the strip kernel takes need
+    `workspace` (gather_tagged_workspace)."""
     n_rows, k = w.shape[0], x.shape[-1]
     if workspace is None and lib().hesa_cuda_gather_tagged_workspace_size(qtype, n_rows, k):
         workspace = gather_tagged_workspace(qtype, n_rows, k, device=x.device)
     arr = (ctypes.c_void_p * (2 * world))(*y_peers)
     _check(lib().hesa_cuda_qmatvec_gather_tagged(qtype, w.data_ptr(), n_rows, k, x.data_ptr(), float(scale), arr,
-                                                 world, sync, workspace.data_ptr() if workspace is not None else None,
+                                                 row0, world, sync,
+                                                 workspace.data_ptr() if workspace is not None else None,
                                                  workspace.numel() if workspace is not None else 0,
                                                  _stream_handle(stream)))
 
 
 def peer_collect(words: int, n: int, parity_stride: int, out, sync: int, stream=None) -> None:
-    """Wait for this step's n tagged words in this rank's buffer (device
-    address `words`, parity 1 `parity_stride` words further), unpack them
-    into out (fp32 device tensor of n values) and advance the step count."""
+    """Wait for this step's n tagged elements in this rank's buffer (device
+    address of word 0 `words`, parity 1 `parity_stride` words further, a
+    multiple of 256), unpack them into out (fp32 device tensor of n values)
+    and advance the step count."""
     import torch
     if out.numel() < n or out.dtype != torch.float32:
         raise ValueError("out must hold n fp32 values")

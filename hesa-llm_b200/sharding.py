@@ -5,11 +5,15 @@ Output rows of y = W x are independent: rank r holds the contiguous rows
 kernel uses between its CTAs), computes y[r0:r1], and the full y is
 all-gathered so every rank holds it. Two ways to gather:
 
-* "peer" (default on GPUs): the matvec kernel itself stores its rows into the
-  gathered buffer of every rank over NVLink (CUDA IPC mappings,
-  hesa_cuda_qmatvec_gather) and one barrier kernel per step publishes
-  completion (hesa_cuda_peer_barrier). No padding: each rank writes at its own
-  row offset.
+* "tagged" (TaggedGather, what the benchmark runs): the matvec kernel itself
+  stores its rows into the gathered buffer of every rank over NVLink (CUDA IPC
+  mappings) as 64-bit words that carry the step's tag
+  (hesa_cuda_qmatvec_gather_tagged), and one collector kernel per step waits
+  until its own buffer holds the step's words (hesa_cuda_peer_collect). No
+  padding: each rank writes at its own row offset.
+* "peer" (PeerGather): the same with fp32 peer stores and one barrier kernel
+  per step publishing completion (hesa_cuda_qmatvec_gather,
+  hesa_cuda_peer_barrier).
 * "nccl": NCCL's all_gather_into_tensor, which wants equal sizes, so every
   rank contributes a slot of ceil(n_out / world) rows and the gathered buffer
   is compacted back to n_out rows with one index_select (a no-op view when
@@ -165,7 +169,7 @@ class TaggedGather:
         if not 1 <= world <= 8 or not 0 <= rank < world:
             raise ValueError(f"bad rank {rank} / world {world}")
         self.out_rows, self.rank, self.world = out_rows, rank, world
-        self.words = _align(8 * out_rows) // 8           # parity stride in words
+        self.words = _align(8 * out_rows, 2048) // 8     # parity stride in words: whole units of 256
         self.sync_off = 2 * 8 * self.words
         self.local, handle = H.peer_alloc(self.sync_off + 256)
         handles = [handle]
@@ -177,9 +181,10 @@ class TaggedGather:
         self.out = torch.empty(out_rows, dtype=torch.float32, device=device)
         self.device = device
 
-    def targets(self, row0: int) -> list[int]:
-        """Addresses (parity-major, then rank) of word `row0` in every rank's buffers."""
-        return [b + par * 8 * self.words + 8 * row0 for par in (0, 1) for b in self.base]
+    def targets(self) -> list[int]:
+        """Word 0 of every rank's buffers (parity-major, then rank); a shard
+        passes its first row's element index with them."""
+        return [b + par * 8 * self.words for par in (0, 1) for b in self.base]
 
     def collect(self, stream=None):
         """End of a step on this rank: the gathered outputs, in self.out."""
@@ -280,7 +285,9 @@ class ShardedDecoder:
         self.ws = H.decode_workspace(self.model, device)
         # one peer allocation per rank: tagged words (8 bytes) of x | a | gate,up
         # | logits, then the token counter
-        sizes = dict(x=8 * D, a=8 * QD, gu=16 * F, logits=8 * V, count=4)
+        # tagged vectors hold whole units of 256 words (the up half of gate|up
+        # starts at element F, a multiple of 256)
+        sizes = dict(x=8 * _align(D), a=8 * _align(QD), gu=16 * _align(F), logits=8 * _align(V), count=4)
         self.off, total = {}, 0
         for name in self.FIELDS:
             self.off[name] = total

@@ -282,15 +282,17 @@ HESA_CUDA_API int hesa_cuda_decode_step(const hesa_cuda_model* model, const hesa
  * tag is the expected one (bounded wait: device status 4 when a peer does not
  * deliver in time) -- no fence, flag array or barrier launch per exchange.
  * The buffers are peer allocations (hesa_cuda_peer_alloc / _open) of 8 bytes
- * per element; arrays are host arrays of `world` device pointers, entry p =
- * rank p's buffer as mapped in this process. The decomposition of the
+ * per element, each vector rounded up to whole units of 256 elements and
+ * stored in the interleaved word order of hesa_cuda_qmatvec_gather_tagged
+ * (16-byte aligned); arrays are host arrays of `world` device pointers,
+ * entry p = rank p's buffer as mapped in this process. The decomposition of the
  * reference's decode loop (docs/architecture.md:277-281) over the GPUs of one
  * node; no counterpart in the reference, which runs on one device. */
 typedef struct {
     int32_t rank, world;
     uint64_t* const* x_peers;       /* [d_model] the residual vector */
     uint64_t* const* a_peers;       /* [n_head * head_dim] attention outputs */
-    uint64_t* const* gu_peers;      /* [2 * d_ff] gate | up */
+    uint64_t* const* gu_peers;      /* [2 * d_ff] gate | up (up at element d_ff) */
     uint64_t* const* logits_peers;  /* [vocab] */
     uint32_t* token_count;          /* this rank's token counter (device uint32, zero-initialised) */
 } hesa_cuda_shard;
@@ -353,29 +355,35 @@ HESA_CUDA_API int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_r
                                            void* stream);
 
 /* The same gathered matvec with every row sent as a tagged 64-bit word
- * (value bits | tag << 32, tag = sync[0] << 12 | 1): row i goes to
- * y_peers[b * world + p][i] for every rank p, b = sync[0] & 1, where sync
- * (device uint32[2], zero-initialised, 8-byte aligned) is this rank's step
- * count and collector ticket. y_peers as for hesa_cuda_qmatvec_gather, 8-byte
- * words instead of floats. Ends with hesa_cuda_peer_collect instead of a
- * barrier: no fence, no flags, and the launch chain stays programmatic.
- * Shapes the row-strip kernel takes (k <= 24576) need no workspace (null,
- * 0); longer rows run the plain matvec into `workspace` (16-byte aligned, at
- * least hesa_cuda_gather_tagged_workspace_size bytes) and one more kernel
- * sends its rows. */
+ * (value bits | tag << 32, tag = sync[0] << 12 | 1): row i of the shard is
+ * element row0 + i of the gathered vector, stored into y_peers[b * world + p]
+ * (host array of 2 * world device pointers: word 0 of rank p's gathered
+ * buffer for parity b, as mapped in this process, 16-byte aligned) for every
+ * rank p, b = sync[0] & 1, where sync (device uint32[2], zero-initialised,
+ * 8-byte aligned) is this rank's step count and collector ticket. Element g
+ * is word ((g & ~255) | ((g >> 1) & 3) << 6 | ((g >> 3) & 31) << 1 | (g & 1))
+ * of a buffer: inside each 256-element unit the words are interleaved so
+ * that the strip kernel's lanes read them with coalesced loads; buffers hold
+ * whole units. Ends with hesa_cuda_peer_collect instead of a barrier: no
+ * fence, no flags, and the launch chain stays programmatic. Shapes the
+ * row-strip kernel takes (k <= 24576) need no workspace (null, 0); longer
+ * rows run the plain matvec into `workspace` (16-byte aligned, at least
+ * hesa_cuda_gather_tagged_workspace_size bytes) and one more kernel sends
+ * its rows. */
 HESA_CUDA_API size_t hesa_cuda_gather_tagged_workspace_size(int qtype, int64_t n_rows, int64_t k);
 HESA_CUDA_API int hesa_cuda_qmatvec_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k,
-                                                  const float* x, float scale, uint64_t* const* y_peers, int world,
-                                                  const uint32_t* sync, void* workspace, size_t workspace_bytes,
-                                                  void* stream);
+                                                  const float* x, float scale, uint64_t* const* y_peers,
+                                                  int64_t row0, int world, const uint32_t* sync, void* workspace,
+                                                  size_t workspace_bytes, void* stream);
 
 /* End of a step of tagged gathered matvecs on this rank: waits until each of
- * the n words of this rank's buffer for the step's parity (words while
- * sync[0] is even, words + parity_stride while odd) carries the step's tag
- * (each wait bounded by the peer wait limit, device status 4 on expiry),
- * writes their values to out[0..n), then advances sync[0]. A gathered result
- * in `out` stays valid until the next collect; the words of a parity may be
- * overwritten from the step after next on. */
+ * the n elements of this rank's buffer for the step's parity (word 0 at
+ * `words` while sync[0] is even, at words + parity_stride while odd;
+ * parity_stride a multiple of 256, at least n rounded up to 256) carries the
+ * step's tag (each wait bounded by the peer wait limit, device status 4 on
+ * expiry), writes their values to out[0..n), then advances sync[0]. A
+ * gathered result in `out` stays valid until the next collect; the words of
+ * a parity may be overwritten from the step after next on. */
 HESA_CUDA_API int hesa_cuda_peer_collect(const uint64_t* words, int64_t n, int64_t parity_stride, float* out,
                                          uint32_t* sync, void* stream);
 

@@ -132,9 +132,10 @@ def test_gathered_matvec_rejects_bad_arguments_without_launching(kwargs, code):
     assert H.lib().hesa_cuda_last_error()
 
 
-def tagged_call(qt=12, w=FAKE, n=64, k=256, x=FAKE, peers=(FAKE,) * 4, world=2, sync=FAKE, ws=None, ws_bytes=0):
+def tagged_call(qt=12, w=FAKE, n=64, k=256, x=FAKE, peers=(FAKE,) * 4, row0=0, world=2, sync=FAKE, ws=None,
+                ws_bytes=0):
     arr = (ctypes.c_void_p * len(peers))(*peers) if peers is not None else None
-    return H.lib().hesa_cuda_qmatvec_gather_tagged(qt, w, n, k, x, 1.0, arr, world, sync, ws, ws_bytes, None)
+    return H.lib().hesa_cuda_qmatvec_gather_tagged(qt, w, n, k, x, 1.0, arr, row0, world, sync, ws, ws_bytes, None)
 
 
 @pytest.mark.parametrize("kwargs,code", [
@@ -145,7 +146,8 @@ def tagged_call(qt=12, w=FAKE, n=64, k=256, x=FAKE, peers=(FAKE,) * 4, world=2, 
     (dict(world=9, peers=(FAKE,) * 18), 2),
     (dict(n=0), 6),
     (dict(k=96, qt=2), 6),
-    (dict(peers=(FAKE, FAKE + 4, FAKE, FAKE)), 2),    # words must be 8-byte aligned
+    (dict(peers=(FAKE, FAKE + 8, FAKE, FAKE)), 2),    # buffers must be 16-byte aligned
+    (dict(row0=-1), 2),
     (dict(k=28672), 2),                                # long rows without the workspace they need
     (dict(k=28672, ws=FAKE, ws_bytes=16), 2),          # ... or with too small a one
 ])
@@ -161,9 +163,10 @@ def test_tagged_gather_workspace_only_for_long_rows():
     assert need >= 4 * 4096 and need % 256 == 0
     assert L.hesa_cuda_gather_tagged_workspace_size(3, 4096, 28672) == 0   # unsupported type
     assert L.hesa_cuda_peer_collect(None, 10, 10, FAKE, FAKE, None) == 2
-    assert L.hesa_cuda_peer_collect(FAKE, 10, 5, FAKE, FAKE, None) == 6    # parities overlap
-    assert L.hesa_cuda_peer_collect(FAKE, 0, 10, FAKE, FAKE, None) == 6
-    assert L.hesa_cuda_peer_collect(FAKE + 4, 10, 10, FAKE, FAKE, None) == 2
+    assert L.hesa_cuda_peer_collect(FAKE, 10, 5, FAKE, FAKE, None) == 6      # parities overlap
+    assert L.hesa_cuda_peer_collect(FAKE, 10, 10, FAKE, FAKE, None) == 6     # not whole units of 256
+    assert L.hesa_cuda_peer_collect(FAKE, 0, 256, FAKE, FAKE, None) == 6
+    assert L.hesa_cuda_peer_collect(FAKE + 8, 10, 256, FAKE, FAKE, None) == 2
 
 
 def test_peer_barrier_and_alloc_reject_bad_arguments():

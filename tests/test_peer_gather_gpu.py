@@ -178,14 +178,14 @@ def test_tagged_world1_matches_plain_matvec_and_replays(torch_cuda):
         blocks.append(b)
         ws.append(torch.from_numpy(b).cuda())
         xs.append(torch.from_numpy(O.gaussian((k,), 1.0, 150 + i)).cuda())
-        tg_targets.append(tg.targets(off))
+        tg_targets.append(off)
         off += n
     stream = torch.cuda.Stream()
 
     def step():
-        for (qt, n, k), w, x, t in zip(mats, ws, xs, tg_targets):
-            H.qmatvec_gather_tagged(qt, w, x, t, 1, tg.sync, scale=0.25, workspace=gws if k > 24576 else None,
-                                    stream=stream)
+        for (qt, n, k), w, x, row0 in zip(mats, ws, xs, tg_targets):
+            H.qmatvec_gather_tagged(qt, w, x, tg.targets(), row0, 1, tg.sync, scale=0.25,
+                                    workspace=gws if k > 24576 else None, stream=stream)
         tg.collect(stream=stream)
 
     want = np.concatenate([O.qmatvec(qt, b, x.cpu().numpy(), scale=0.25) for (qt, n, k), b, x in
@@ -233,7 +233,7 @@ def test_tagged_collect_wait_runs_out_and_reports_status_4(torch_cuda):
     b = O.quantize(qt, O.gaussian((n, k), 0.02, 160))
     x = O.gaussian((k,), 1.0, 161)
     w = torch.from_numpy(b).cuda()
-    H.qmatvec_gather_tagged(qt, w, torch.from_numpy(x).cuda(), tg.targets(0), 1, tg.sync)
+    H.qmatvec_gather_tagged(qt, w, torch.from_numpy(x).cuda(), tg.targets(), 0, 1, tg.sync)
     y = tg.collect()
     torch.cuda.synchronize()
     assert rel_l2(y.cpu().numpy(), O.qmatvec(qt, b, x)) <= REL_L2_TOL
@@ -299,14 +299,14 @@ def _tagged_rank_main(rank, world, port, out_dir):
         for i, (qt, n, k) in enumerate(mats):
             blocks = Orc.quantize(qt, Orc.gaussian((n, k), 0.02, 170 + i))
             r0, r1 = S.row_range(n, rank, world)
-            shards.append((qt, n, k, blocks, torch.from_numpy(blocks[r0:r1]).cuda(), tg.targets(off + r0)))
+            shards.append((qt, n, k, blocks, torch.from_numpy(blocks[r0:r1]).cuda(), off + r0))
             off += n
         dist.barrier()
         errs = []
         for step in range(4):    # both parities twice, ranks not in lockstep between steps
             xs = [Orc.gaussian((k,), 1.0, 180 + 10 * step + i) for i, (_, _, k) in enumerate(mats)]
-            for (qt, n, k, blocks, w, t), x in zip(shards, xs):
-                H.qmatvec_gather_tagged(qt, w, torch.from_numpy(x).cuda(), t, world, tg.sync)
+            for (qt, n, k, blocks, w, row0), x in zip(shards, xs):
+                H.qmatvec_gather_tagged(qt, w, torch.from_numpy(x).cuda(), tg.targets(), row0, world, tg.sync)
             y = tg.collect().cpu().numpy()
             want = np.concatenate([Orc.qmatvec(qt, blocks, x) for (qt, n, k, blocks, w, t), x in zip(shards, xs)])
             errs.append(rel_l2(y, want))
