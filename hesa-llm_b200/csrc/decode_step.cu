@@ -275,7 +275,11 @@ __global__ void __launch_bounds__(1024) ll_fill_kernel(const float* __restrict__
                                                        uint32_t* count) {
     const uint32_t c = *reinterpret_cast<volatile uint32_t*>(count) + 1u;
     const uint32_t tag = (c << 12) | lo_of(0, kPhEmbed);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) st_ll(x_ll + ll_pos(i), x[i], tag);
+    const int n_words = (n + 255) & ~255;
+    for (int w = threadIdx.x; w < n_words; w += blockDim.x) {
+        const int e = static_cast<int>(ll_elem(w));
+        if (e < n) st_ll(x_ll + w, x[e], tag);
+    }
     __syncthreads();
     if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(count) = c;
 }

@@ -455,12 +455,18 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         rtag = (x_tag & ~0xFFFu) | lin.resid_lo;
     }
     if constexpr (OUT == kOutTagged) out_tag = ll_tag(lout.count, lout.lo);
-    // the residual word of this thread's first row, read now (it arrived with
-    // the input of an earlier kernel) and checked in the epilogue
+    // The tagged epilogue walks the words of this CTA's rows in word order
+    // (consecutive threads, consecutive words: whole lines over NVLink) --
+    // rows [ra, rb) of the shard are elements voff + ra .. of the output.
+    // The residual word of this thread's first row is read now (it arrived
+    // with the input of an earlier kernel) and checked in the epilogue.
     uint64_t resid_w = 0;
     if constexpr (LLX && OUT == kOutTagged) {
-        if (lin.resid && static_cast<int>(threadIdx.x) < nrows)
-            resid_w = ld_ll(lin.resid + ll_pos(lin.resid_off + r0 + static_cast<int>(threadIdx.x)));
+        if (lin.resid) {
+            const int64_t A = lout.off + r0, B = lout.off + r1;
+            const int64_t e = ll_elem((A & ~int64_t(255)) + threadIdx.x);
+            if (e >= A && e < B) resid_w = ld_ll(lin.resid + ll_pos(lin.resid_off + (e - lout.off)));
+        }
     }
 
     // x as digit planes, converted once per CTA (one warp per unit of 256;
@@ -615,24 +621,34 @@ qmv_strip_kernel(const uint8_t* __restrict__ w, int n_out, int k, const float* _
         // decode step, tagged gather)
         const uint32_t tag = out_tag;
         const bool odd = lout.by_parity && ((tag >> 12) & 1u);
-        for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
-            float s = 0.f;
-            for (int t = 0; t < wps; ++t) s += part[i * wps + t];
-            const int row = r0 + i;
-            float val = s * scale;
-            if constexpr (LLX) {
-                if (lin.resid) {
-                    const uint64_t* ra = lin.resid + ll_pos(lin.resid_off + row);
-                    const float rv = i == static_cast<int>(threadIdx.x)
-                                         ? ll_value(ra, resid_w, rtag, lin.limit_ns, status, &s_ll_failed)
-                                         : ld_ll_wait(ra, rtag, lin.limit_ns, status, &s_ll_failed);
-                    val = __fadd_rn(rv, val);
+        auto emit = [&](int ra, int rb, int64_t voff, uint64_t* const* bufs) {
+            if (ra >= rb) return;
+            const int64_t A = voff + ra, B = voff + rb;
+            const int64_t w1 = (B + 255) & ~int64_t(255);
+            bool first = true;
+            for (int64_t w = (A & ~int64_t(255)) + threadIdx.x; w < w1; w += blockDim.x, first = false) {
+                const int64_t e = ll_elem(w);
+                if (e < A || e >= B) continue;
+                const int row = static_cast<int>(e - voff), i = row - r0;
+                float s = 0.f;
+                for (int t = 0; t < wps; ++t) s += part[i * wps + t];
+                float val = s * scale;
+                if constexpr (LLX) {
+                    if (lin.resid) {
+                        const uint64_t* rp = lin.resid + ll_pos(lin.resid_off + row);
+                        const float rv = first ? ll_value(rp, resid_w, rtag, lin.limit_ns, status, &s_ll_failed)
+                                               : ld_ll_wait(rp, rtag, lin.limit_ns, status, &s_ll_failed);
+                        val = __fadd_rn(rv, val);
+                    }
                 }
+                for (int p = 0; p < lout.world; ++p) st_ll(bufs[p] + w, val, tag);
             }
-            const bool second = !lout.by_parity && row >= lout.split;
-            const int64_t at = second ? ll_pos(lout.off2 + (row - lout.split)) : ll_pos(lout.off + row);
-            for (int p = 0; p < lout.world; ++p)
-                st_ll(((lout.by_parity ? odd : second) ? lout.y2[p] : lout.y[p]) + at, val, tag);
+        };
+        if (lout.by_parity) {
+            emit(r0, r1, lout.off, odd ? lout.y2 : lout.y);
+        } else {
+            emit(r0, min(r1, lout.split), lout.off, lout.y);
+            emit(max(r0, lout.split), r1, lout.off2 - lout.split, lout.y2);
         }
     } else if constexpr (OUT == kOutPlain) {
         for (int i = threadIdx.x; i < nrows; i += blockDim.x) {
