@@ -564,16 +564,37 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None, rank: int = 0, wor
     tok_dev = torch.tensor([1234], dtype=torch.int32, device=dev)
     dec = None
     want = None
+    replica_ms = None
     if world > 1:
         import sharding
         # the unsharded step on this rank's full copy: the sharded step computes
         # every row with the same summation order, so its logits must equal
-        # these bit for bit
-        H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok_dev, out=x, stream=stream)
+        # these bit for bit; timed too (one independent sequence per GPU)
         want = torch.empty_like(logits)
-        H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos_dev, want, d["ws"],
-                      stream=stream)
-        stream.synchronize()
+
+        def replica():
+            H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok_dev, out=x, stream=stream)
+            H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos_dev, want, d["ws"],
+                          stream=stream)
+
+        with torch.cuda.stream(stream):
+            replica()
+            stream.synchronize()
+            g_rep = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_rep, stream=stream):
+                replica()
+            for _ in range(3):
+                g_rep.replay()
+            stream.synchronize()
+            r0 = torch.cuda.Event(enable_timing=True)
+            r1 = torch.cuda.Event(enable_timing=True)
+            r0.record(stream)
+            for _ in range(steps):
+                g_rep.replay()
+            r1.record(stream)
+            r1.synchronize()
+            replica_ms = r0.elapsed_time(r1) / steps
+            del g_rep
         dec = sharding.ShardedDecoder(cfg, d, rank, world, device=dev)
         logits = dec.logits()
         del d["layers"], d["arr"]   # the full model's weights: every rank keeps its shards only
@@ -618,7 +639,7 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None, rank: int = 0, wor
         pg.barrier()
         dec.close()
         pg.barrier()
-    return dict(ms=ms, finite=ok, equal_unsharded=same, bytes_token=d["bytes_token"], weight_bytes=d["weight_bytes"],
+    return dict(ms=ms, finite=ok, equal_unsharded=same, replica_ms=replica_ms, bytes_token=d["bytes_token"], weight_bytes=d["weight_bytes"],
                 kv_bytes=d["kv_bytes"])
 
 
@@ -662,6 +683,31 @@ def profile_batched(steps: int, batch: int):
         H.qmatvec(QT["Q4_K"], w, x, y=y, workspace=ws)
     torch.cuda.synchronize()
     log(f"profile batched done: {steps} launch(es) of B={batch}, outputs finite: {bool(torch.isfinite(y).all())}")
+    return 0
+
+
+def profile_shapes(steps: int):
+    """A few eager launches of the shapes outside the sweep, for ncu: the
+    Q4_0 4096 x 4096 matvec (batch 1, row-strip kernel) and the 70B down
+    projection, Q4_K 8192 x 28672 (rows longer than the strip kernel takes:
+    the split-row streaming kernel). One weight copy of each (9.4 + 132 MB)."""
+    import torch
+    import hesa_cuda as H
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4040)
+    out = []
+    for qt, n, k in ((QT["Q4_0"], 4096, 4096), (QT["Q4_K"], 8192, 28672)):
+        w = H.quantize(qt, torch.randn((n, k), generator=g, device=dev).mul_(0.02))
+        x = torch.randn(k, generator=g, device=dev)
+        y = torch.empty(n, device=dev)
+        ws = H.make_workspace(qt, n, k, device=dev)
+        for _ in range(max(steps, 1)):
+            H.qmatvec(qt, w, x, y=y, workspace=ws)
+        out.append(y)
+    torch.cuda.synchronize()
+    log(f"profile shapes done: {steps} launch(es) each, outputs finite: "
+        f"{all(bool(torch.isfinite(y).all()) for y in out)}")
     return 0
 
 
@@ -944,12 +990,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     # max over ranks
     times = torch.tensor([dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec["ms"], nccl_ms or 0.0,
                           0.0 if peers is None or gathered_ok else 1.0, p70_ms,
-                          0.0 if dec["equal_unsharded"] in (None, True) else 1.0, p70_local_ms],
+                          0.0 if dec["equal_unsharded"] in (None, True) else 1.0, p70_local_ms,
+                          dec["replica_ms"] or 0.0],
                          dtype=torch.float64, device=dev)
     if pg is not None:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
-    dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms, nccl_ms, gather_bad, p70_ms, dec_bad, p70_local_ms = (
-        float(v) for v in times.cpu())
+    (dt_ms, kernel_ms, e2e_ms, e2e_eager_ms, dec_ms, nccl_ms, gather_bad, p70_ms, dec_bad, p70_local_ms,
+     replica_ms) = (float(v) for v in times.cpu())
 
     if rank == 0:
         bytes_step = step_bytes() * world
@@ -1005,7 +1052,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                        "timing": "embedding lookup + 32 layers + LM head captured as one CUDA graph per token, "
                                  "replayed between CUDA events",
                        "logits_finite": dec["finite"],
-                       "logits_equal_unsharded_step": (dec_bad == 0.0) if world > 1 else None},
+                       "logits_equal_unsharded_step": (dec_bad == 0.0) if world > 1 else None,
+                       "independent_sequences": ({"tokens_per_s": round(world * 1000.0 / replica_ms, 1),
+                                                  "ms_per_token": round(replica_ms, 4),
+                                                  "how": f"the unsharded step of one sequence on each of the {world} "
+                                                         "GPUs at once (max over ranks)"}
+                                                 if world > 1 else None)},
             "batched": {"workload": "Q4_K [n_out x k] times B activation rows (batched decode), "
                                     "one launch per 16 rows on the tensor cores (B >= 3; B = 2 as two batch-1 passes)",
                         "us_and_gbs": batched,
@@ -1052,6 +1104,9 @@ def main():
     ap.add_argument("--profile-decode", action="store_true",
                     help="untimed: a 2-layer model of the 7B decode shapes, --steps eager decode steps "
                          "(for ncu launch lists of one step)")
+    ap.add_argument("--profile-shapes", action="store_true",
+                    help="untimed: --steps eager launches each of Q4_0 4096x4096 and Q4_K 8192x28672 "
+                         "(for ncu captures of the shapes outside the sweep)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus else 1)))
@@ -1062,6 +1117,8 @@ def main():
         return run_reference(args, rank, world)
     if args.profile_decode:
         return profile_decode(args.steps)
+    if args.profile_shapes:
+        return profile_shapes(args.steps)
     if args.profile_batched:
         return profile_batched(args.steps, args.profile_batched)
     return run_gpu(args, rank, world, local_rank)
