@@ -6,6 +6,7 @@
 // per host thread.
 #include "../../include/hesa_cuda.h"
 #include "abi_errors.h"
+#include "trace.h"
 #include "qmatvec.h"
 #include "qmm.h"
 #include "quantize.h"
@@ -60,6 +61,7 @@ size_t hesa_cuda_qmatvec_workspace_size(int qtype, int64_t n_out, int64_t k, int
 int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx,
                       int64_t batch, float* y, int64_t ldy, float scale, void* workspace,
                       size_t workspace_bytes, void* stream) {
+    HESA_TRACE("hesa_cuda_qmatvec");
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w || !x || !y) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n_out <= 0 || k <= 0 || batch <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "non-positive dimension");
@@ -108,6 +110,7 @@ int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int64_t k, const 
 
 int hesa_cuda_dequantize(int qtype, const void* w, int64_t n_rows, int64_t k, float* out, int64_t ldo,
                          void* stream) {
+    HESA_TRACE("hesa_cuda_dequantize");
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w || !out) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n_rows <= 0 || k <= 0 || k % hesa_cuda::block_elems(qtype) != 0 || ldo < k)
@@ -119,6 +122,7 @@ int hesa_cuda_dequantize(int qtype, const void* w, int64_t n_rows, int64_t k, fl
 
 int hesa_cuda_quantize(int qtype, const float* src, int64_t n_rows, int64_t k, int64_t ld_src, void* dst,
                        void* stream) {
+    HESA_TRACE("hesa_cuda_quantize");
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!src || !dst) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n_rows <= 0 || k <= 0 || k % hesa_cuda::block_elems(qtype) != 0 || ld_src < k)
@@ -169,6 +173,7 @@ int hesa_cuda_peer_close(void* dev_ptr) {
 
 int hesa_cuda_qmatvec_gather(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,
                              float* const* y_peers, int world, const uint32_t* epoch, void* stream) {
+    HESA_TRACE("hesa_cuda_qmatvec_gather");
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w || !x || !y_peers || !epoch) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (world < 1 || world > hesa_cuda::kMaxPeers) return fail(HESA_CUDA_INVALID_ARGUMENT, "world must be 1..8");
@@ -206,6 +211,7 @@ size_t hesa_cuda_gather_tagged_workspace_size(int qtype, int64_t n_rows, int64_t
 int hesa_cuda_qmatvec_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x,
                                     float scale, uint64_t* const* y_peers, int64_t row0, int world,
                                     const uint32_t* sync, void* workspace, size_t workspace_bytes, void* stream) {
+    HESA_TRACE("hesa_cuda_qmatvec_gather_tagged");
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w || !x || !y_peers || !sync) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (row0 < 0 || row0 >= (int64_t(1) << 40)) return fail(HESA_CUDA_INVALID_ARGUMENT, "bad row offset");
@@ -250,6 +256,7 @@ int hesa_cuda_qmatvec_gather_tagged(int qtype, const void* w, int64_t n_rows, in
 
 int hesa_cuda_peer_collect(const uint64_t* words, int64_t n, int64_t parity_stride, float* out, uint32_t* sync,
                            void* stream) {
+    HESA_TRACE("hesa_cuda_peer_collect");
     if (!words || !out || !sync) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n <= 0 || n >= (int64_t(1) << 30)) return fail(HESA_CUDA_SHAPE_MISMATCH, "word count must be 1 .. 2^30 - 1");
     if (parity_stride < ((n + 255) & ~int64_t(255)) || parity_stride % 256 != 0)
@@ -262,6 +269,7 @@ int hesa_cuda_peer_collect(const uint64_t* words, int64_t n, int64_t parity_stri
 }
 
 int hesa_cuda_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch, void* stream) {
+    HESA_TRACE("hesa_cuda_peer_barrier");
     if (!flags || !epoch) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (world < 1 || world > hesa_cuda::kMaxPeers || rank < 0 || rank >= world)
         return fail(HESA_CUDA_INVALID_ARGUMENT, "bad rank / world");
@@ -308,6 +316,7 @@ extern "C" {
 
 int hesa_cuda_matmul_f32(const float* a, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
                          float* y, int64_t ldy, float scale, void* stream) {
+    HESA_TRACE("hesa_cuda_matmul_f32");
     if (!a || !x || !y) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n_out <= 0 || k <= 0 || batch <= 0 || ldx < k || (batch > 1 && ldy < n_out) ||
         n_out >= (int64_t(1) << 31) || k >= (int64_t(1) << 31))
@@ -400,6 +409,7 @@ size_t hesa_cuda_attention_workspace_size(int64_t n_head, int64_t head_dim, int6
 int hesa_cuda_attention(const float* q, const void* k_cache, const void* v_cache, float* out, int64_t n_head,
                         int64_t n_kv_head, int64_t head_dim, int64_t ctx, const int32_t* pos_dev, int32_t pos_host,
                         void* workspace, size_t workspace_bytes, void* stream) {
+    HESA_TRACE("hesa_cuda_attention");
     if (!q || !k_cache || !v_cache || !out || !workspace) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (!aligned16(k_cache) || !aligned16(v_cache))
         return fail(HESA_CUDA_INVALID_ARGUMENT, "KV caches must be 16-byte aligned");
@@ -424,6 +434,7 @@ int hesa_cuda_attention(const float* q, const void* k_cache, const void* v_cache
 extern "C" int hesa_cuda_qmatvec_noalloc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x,
                                          int64_t ldx, int64_t batch, float* y, int64_t ldy, float scale,
                                          void* stream) {
+    HESA_TRACE("hesa_cuda_qmatvec_noalloc");
     if (!hesa_cuda::qtype_supported(qtype)) return fail(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w || !x || !y) return fail(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     if (n_out <= 0 || k <= 0 || batch <= 0) return fail(HESA_CUDA_SHAPE_MISMATCH, "non-positive dimension");

@@ -20,6 +20,7 @@
 // every token.
 #include "../../include/hesa_cuda.h"
 #include "abi_errors.h"
+#include "trace.h"
 #include "decode_ops.h"
 #include "hesa_common.cuh"
 #include "qmatvec.h"
@@ -108,6 +109,7 @@ size_t hesa_cuda_decode_workspace_size(const hesa_cuda_model* m) {
 
 int hesa_cuda_embed(int qtype, const void* w_emb, int64_t vocab, int64_t d_model, const int32_t* token_dev,
                     float* x, void* stream) {
+    HESA_TRACE("hesa_cuda_embed");
     using namespace hesa_cuda;
     if (!qtype_supported(qtype)) return record_error(HESA_CUDA_BACKEND_NOT_AVAILABLE, "unsupported qtype");
     if (!w_emb || !token_dev || !x) return record_error(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
@@ -134,6 +136,7 @@ int hesa_cuda_decode_step(const hesa_cuda_model* m, const hesa_cuda_layer* layer
                           const void* w_out, const float* rope_table, int32_t rope_rows, const float* x_embed,
                           const int32_t* pos_dev, float* logits, void* workspace, size_t workspace_bytes,
                           void* stream) {
+    HESA_TRACE("hesa_cuda_decode_step");
     using hesa_cuda::record_error;
     if (!hesa_cuda::model_ok(m)) return record_error(HESA_CUDA_SHAPE_MISMATCH, "bad model shape");
     if (!layers || !out_norm || !w_out || !rope_table || !x_embed || !pos_dev || !logits || !workspace)
@@ -308,6 +311,7 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
                                              const float* rope_table, int32_t rope_rows, const float* x_embed,
                                              const int32_t* pos_dev, float* logits, void* workspace,
                                              size_t workspace_bytes, void* stream) {
+    HESA_TRACE("hesa_cuda_decode_step_sharded");
     using namespace hesa_cuda;
     if (!model_ok(m)) return record_error(HESA_CUDA_SHAPE_MISMATCH, "bad model shape");
     if (!sh || !layers || !out_norm || !w_out || !rope_table || !x_embed || !pos_dev || !logits || !workspace)

@@ -1,5 +1,5 @@
-// strip_core.cuh -- the decode core shared by the batch-1 row-strip kernels
-// (qmatvec.cu: one matvec per launch; qmv_chain.cu: several per launch):
+// strip_core.cuh -- the decode core of the batch-1 row-strip kernel
+// (qmatvec.cu, every input and output mode):
 // the digit-plane form of x in shared memory, the per-type integer dot
 // products of one quarter of a 256-weight unit, and the warp reductions.
 //

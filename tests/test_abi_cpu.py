@@ -191,3 +191,23 @@ def test_peer_wait_limit_setting_is_host_side_and_bounded():
     assert L.hesa_cuda_set_peer_wait_limit_us(61 * 1000 * 1000) == 2   # above a minute
     assert L.hesa_cuda_set_peer_wait_limit_us(50 * 1000) == 0
     assert L.hesa_cuda_set_peer_wait_limit_us(0) == 0                  # back to the 2 s default
+
+
+def test_nvtx_tracing_switch_leaves_calls_unchanged():
+    """HESA_CUDA_NVTX=1 wraps the entry points in NVTX ranges (no tool
+    attached here: the ranges are no-ops); argument checks and error codes
+    are the same with it on."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path[:0] = ['hesa-llm_b200']\n"
+            "import ctypes, hesa_cuda as H\n"
+            "L = H.lib()\n"
+            "rc = L.hesa_cuda_qmatvec(3, 1 << 20, 64, 256, 1 << 20, 256, 1, 1 << 20, 64, 1.0, None, 0, None)\n"
+            "rc2 = L.hesa_cuda_peer_collect(None, 10, 256, 1 << 20, 1 << 20, None)\n"
+            "print(rc, rc2)\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for env in ({"HESA_CUDA_NVTX": "1"}, {"HESA_CUDA_NVTX": "0"}):
+        out = subprocess.run([sys.executable, "-c", code], cwd=root, env={**os.environ, **env},
+                             capture_output=True, text=True, timeout=300)
+        assert out.returncode == 0, out.stderr
+        assert out.stdout.split() == ["3", "2"], out.stdout
