@@ -553,7 +553,8 @@ def run_decode(dev, stream, steps: int, warmup: int, pg=None, rank: int = 0, wor
     """tokens/s of the 7B-shaped Q4_K decode step (embedding lookup + every
     layer + LM head) of ONE sequence, one CUDA graph per token, device-timed.
     At N > 1 the sequence is decoded on all N GPUs together: heads, KV caches
-    and row shares of every projection per rank (sharding.ShardedDecoder)."""
+    and row shares of gate|up and the LM head per rank, Wo and W_down whole on
+    every rank (sharding.ShardedDecoder)."""
     import torch
     import hesa_cuda as H
     cfg = DECODE_7B
@@ -1045,9 +1046,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                        "bytes_per_token": dec["bytes_token"],
                        "gbs": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9, 1),
                        "frac_of_hbm": round(dec["bytes_token"] / (dec_ms * 1e-3) / 1e9 / (peak * world), 4),
-                       "parallelism": (f"one sequence on {world} GPUs: heads, KV caches and row shares of every "
-                                       "projection per rank, the four gathers per layer fused into the kernels "
-                                       "(tagged 64-bit peer stores, waited for per word by the next kernel)"
+                       "parallelism": (f"one sequence on {world} GPUs: heads, KV caches and row shares of gate|up and "
+                                       "the LM head per rank, Wo and W_down whole on every rank; the two exchanges "
+                                       "per layer fused into the producing kernels (tagged 64-bit peer stores, "
+                                       "waited for per word by the next kernel)"
                                        if world > 1 else "single GPU"),
                        "timing": "embedding lookup + 32 layers + LM head captured as one CUDA graph per token, "
                                  "replayed between CUDA events",

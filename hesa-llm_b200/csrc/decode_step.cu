@@ -264,25 +264,33 @@ int hesa_cuda_decode_step(const hesa_cuda_model* m, const hesa_cuda_layer* layer
 // ---------------------------------------------------------------------------
 // head-sharded decode step
 // ---------------------------------------------------------------------------
+//
+// Rank r of W holds the Q, K, V rows of its heads (and their KV caches), its
+// row shares of gate|up and of the LM head, and all of Wo and W_down; the
+// residual x stays local and plain on every rank. Per layer two vectors are
+// exchanged, as tagged words (peer_sync.cuh): the attention output (each rank
+// its heads) and gate|up (each rank its rows). Every rank then computes all
+// rows of Wo and W_down itself -- 35 MB of the 113 MB of a 7B Q4_K layer --
+// instead of exchanging the residual twice more: at batch 1 a launch's fixed
+// cost (grid wait, staging of x, epilogue, the wait for the slowest rank)
+// is worth more than those bytes (measured, 7B: the four-exchange form took
+// 1.84 and 2.04 ms per token on 2 and 4 GPUs against 1.74 on one). Every
+// output row is summed as in the unsharded step, so the logits are its
+// logits bit for bit.
 
 namespace hesa_cuda {
 namespace {
 
-// Tag low bits of the step's exchanges: (layer << 3) | phase.
-enum : uint32_t { kPhEmbed = 0, kPhAttn = 1, kPhWo = 2, kPhGateUp = 3, kPhDown = 4, kPhLogits = 5 };
+// Tag low bits of the step's exchanges: (layer << 3) | phase (never 0).
+enum : uint32_t { kPhAttn = 1, kPhGateUp = 3, kPhLogits = 5 };
 constexpr uint32_t lo_of(int64_t layer, uint32_t phase) { return (static_cast<uint32_t>(layer) << 3) | phase; }
 
-// The token's embedding into this rank's tagged residual buffer; opens the
-// token (one CTA: every thread reads the old count, then it is advanced).
-__global__ void __launch_bounds__(1024) ll_fill_kernel(const float* __restrict__ x, uint64_t* x_ll, int n,
-                                                       uint32_t* count) {
+// The token's embedding into the plain residual; opens the token (one CTA:
+// every thread reads the old count, then it is advanced).
+__global__ void __launch_bounds__(1024) shard_begin_kernel(const float* __restrict__ x_embed, float* __restrict__ x,
+                                                           int n, uint32_t* count) {
     const uint32_t c = *reinterpret_cast<volatile uint32_t*>(count) + 1u;
-    const uint32_t tag = (c << 12) | lo_of(0, kPhEmbed);
-    const int n_words = (n + 255) & ~255;
-    for (int w = threadIdx.x; w < n_words; w += blockDim.x) {
-        const int e = static_cast<int>(ll_elem(w));
-        if (e < n) st_ll(x_ll + w, x[e], tag);
-    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = x_embed[i];
     __syncthreads();
     if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(count) = c;
 }
@@ -318,13 +326,13 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
         return record_error(HESA_CUDA_INVALID_ARGUMENT, "null pointer");
     const int W = sh->world, r = sh->rank;
     if (W < 1 || W > kPeerSyncMax || r < 0 || r >= W) return record_error(HESA_CUDA_INVALID_ARGUMENT, "bad rank / world");
-    if (!sh->x_peers || !sh->a_peers || !sh->gu_peers || !sh->logits_peers || !sh->token_count)
+    if (!sh->a_peers || !sh->gu_peers || !sh->logits_peers || !sh->token_count)
         return record_error(HESA_CUDA_INVALID_ARGUMENT, "null shard buffer array");
     for (int p = 0; p < W; ++p) {
-        if (!sh->x_peers[p] || !sh->a_peers[p] || !sh->gu_peers[p] || !sh->logits_peers[p])
+        if (!sh->a_peers[p] || !sh->gu_peers[p] || !sh->logits_peers[p])
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "null peer buffer");
-        if ((reinterpret_cast<uintptr_t>(sh->x_peers[p]) | reinterpret_cast<uintptr_t>(sh->a_peers[p]) |
-             reinterpret_cast<uintptr_t>(sh->gu_peers[p]) | reinterpret_cast<uintptr_t>(sh->logits_peers[p])) & 15)
+        if ((reinterpret_cast<uintptr_t>(sh->a_peers[p]) | reinterpret_cast<uintptr_t>(sh->gu_peers[p]) |
+             reinterpret_cast<uintptr_t>(sh->logits_peers[p])) & 15)
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "peer buffers must be 16-byte aligned");
     }
     if (m->n_head % W != 0 || m->n_kv_head % W != 0)
@@ -344,20 +352,19 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
         a = n * r / W;
         b = n * (r + 1) / W;
     };
-    int64_t d0, d1, f0, f1, v0, v1;
-    share(D, d0, d1);
+    int64_t f0, f1, v0, v1;
     share(F, f0, f1);
     share(V, v0, v1);
     const size_t rb_d = hesa_cuda_row_bytes(qt, D), rb_qd = hesa_cuda_row_bytes(qt, QD),
                  rb_f = hesa_cuda_row_bytes(qt, F);
     if (!rb_d || !rb_qd || !rb_f)
         return record_error(HESA_CUDA_SHAPE_MISMATCH, "d_model, n_head*head_dim and d_ff must be block multiples");
-    if (d1 <= d0 || f1 <= f0 || v1 <= v0) return record_error(HESA_CUDA_SHAPE_MISMATCH, "an empty row share");
+    if (f1 <= f0 || v1 <= v0) return record_error(HESA_CUDA_SHAPE_MISMATCH, "an empty row share");
     using SI = StripInput;
     if (!qmv_strip_fused_eligible(qt, layers[0].wq, qd_r + 2 * kd_r, D, SI::kRmsNorm) ||
-        !qmv_strip_fused_eligible(qt, layers[0].wo, d1 - d0, QD, SI::kPlain) ||
+        !qmv_strip_fused_eligible(qt, layers[0].wo, D, QD, SI::kPlain) ||
         !qmv_strip_fused_eligible(qt, layers[0].w_gate, 2 * (f1 - f0), D, SI::kRmsNorm) ||
-        !qmv_strip_fused_eligible(qt, layers[0].w_down, d1 - d0, F, SI::kSiluMul) ||
+        !qmv_strip_fused_eligible(qt, layers[0].w_down, D, F, SI::kSiluMul) ||
         !qmv_strip_fused_eligible(qt, w_out, v1 - v0, D, SI::kRmsNorm))
         return record_error(HESA_CUDA_SHAPE_MISMATCH, "a shard does not fit the row-strip kernel");
     if ((HD != 64 && HD != 128 && HD != 256) || m->ctx > 131072)
@@ -367,54 +374,46 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
     if (e != cudaSuccess) return record_cuda_error(e, "status word");
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* x = reinterpret_cast<float*>(ws + L.x);
     float* q = reinterpret_cast<float*>(ws + L.qkv);
     float* k = q + qd_r;
     float* v = k + kd_r;
     void* att_ws = ws + L.att;
-    uint64_t* x_own = sh->x_peers[r];
     const uint32_t* cnt = sh->token_count;
     const unsigned long long limit_ns = peer_wait_limit();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-    // vectors by their word 0; the residual's rows of this shard start at
-    // element resid_off
-    auto in = [&](const uint64_t* x, uint32_t x_lo, const uint64_t* resid, int64_t resid_off, uint32_t resid_lo) {
+    // a tagged input vector (by its word 0)
+    auto in = [&](const uint64_t* xt, uint32_t lo) {
         LLIn li = {};
-        li.x = x;
-        li.resid = resid;
-        li.resid_off = resid_off;
+        li.x = xt;
         li.count = cnt;
-        li.x_lo = x_lo;
-        li.resid_lo = resid_lo;
+        li.x_lo = lo;
         li.limit_ns = limit_ns;
         return li;
     };
     // this rank's rows are elements off.. of every rank's vector (rows from
-    // `split` on: elements off2.. of bufs2)
-    auto out = [&](uint64_t* const* bufs, int64_t off, int64_t n_rows, uint64_t* const* bufs2, int64_t off2,
-                   int64_t split, uint32_t lo) {
+    // `split` on: elements off2..)
+    auto out = [&](uint64_t* const* bufs, int64_t off, int64_t n_rows, int64_t off2, int64_t split, uint32_t lo) {
         LLOut o = {};
-        for (int p = 0; p < W; ++p) {
-            o.y[p] = bufs[p];
-            o.y2[p] = bufs2 ? bufs2[p] : nullptr;
-        }
+        for (int p = 0; p < W; ++p) o.y[p] = o.y2[p] = bufs[p];
         o.off = off;
         o.off2 = off2;
-        o.split = static_cast<int>(bufs2 ? split : n_rows);
+        o.split = static_cast<int>(split < n_rows ? split : n_rows);
         o.world = W;
         o.count = cnt;
         o.lo = lo;
         return o;
     };
-    auto strip = [&](const void* w, int64_t n, int64_t kk, SI mode, const float* nw, float* y, const LLIn& li,
-                     const LLOut& lo, const char* what) {
-        const cudaError_t ce = qmv_strip_shard(qt, w, n, kk, mode, nw, m->rms_eps, 1.0f, y, li, lo, s);
+    auto strip = [&](const void* w, int64_t n, int64_t kk, SI mode, const float* nw, const float* xp, float* y,
+                     const float* resid, const LLIn& li, const LLOut& lo, const char* what) {
+        const cudaError_t ce = qmv_strip_shard(qt, w, n, kk, mode, nw, m->rms_eps, 1.0f, xp, y, resid, li, lo, s);
         return ce == cudaSuccess ? HESA_CUDA_OK : record_cuda_error(ce, what);
     };
 
-    ll_fill_kernel<<<1, 1024, 0, s>>>(x_embed, x_own, static_cast<int>(D), sh->token_count);
+    shard_begin_kernel<<<1, 1024, 0, s>>>(x_embed, x, static_cast<int>(D), sh->token_count);
     e = cudaGetLastError();
-    if (e != cudaSuccess) return record_cuda_error(e, "embedding fill");
+    if (e != cudaSuccess) return record_cuda_error(e, "token start");
     uint64_t* a_out[kPeerSyncMax] = {};
     for (int p = 0; p < W; ++p) a_out[p] = sh->a_peers[p];
     int rc = HESA_CUDA_OK;
@@ -429,36 +428,30 @@ extern "C" int hesa_cuda_decode_step_sharded(const hesa_cuda_model* m, const hes
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "Q|K|V and gate|up shards must be joined");
         if ((reinterpret_cast<uintptr_t>(Ly.k_cache) & 15) || (reinterpret_cast<uintptr_t>(Ly.v_cache) & 15))
             return record_error(HESA_CUDA_INVALID_ARGUMENT, "KV caches must be 16-byte aligned");
-        // the residual as the previous exchange left it
-        const uint32_t x_lo = l == 0 ? lo_of(0, kPhEmbed) : lo_of(l - 1, kPhDown);
         // q|k|v of this rank's heads (local)
-        rc = strip(Ly.wq, qd_r + 2 * kd_r, D, SI::kRmsNorm, Ly.attn_norm, q, in(x_own, x_lo, nullptr, 0, 0), LLOut{},
+        rc = strip(Ly.wq, qd_r + 2 * kd_r, D, SI::kRmsNorm, Ly.attn_norm, x, q, nullptr, LLIn{}, LLOut{},
                    "sharded q|k|v");
         if (rc) break;
         // attention of this rank's heads -> every rank's a
         e = attention_rope_shard(q, k, v, Ly.k_cache, Ly.v_cache, nullptr, hl, kvl, HD, rope_table, rope_rows, m->ctx,
                                  pos_dev, att_ws, a_out, r * qd_r, W, cnt, lo_of(l, kPhAttn), s);
         if (e != cudaSuccess) return record_cuda_error(e, "sharded attention");
-        // x[d0:d1] += Wo a -> every rank's x
-        rc = strip(Ly.wo, d1 - d0, QD, SI::kPlain, nullptr, nullptr,
-                   in(sh->a_peers[r], lo_of(l, kPhAttn), x_own, d0, x_lo),
-                   out(sh->x_peers, d0, d1 - d0, nullptr, 0, 0, lo_of(l, kPhWo)), "sharded Wo");
+        // x += Wo a, all rows (local)
+        rc = strip(Ly.wo, D, QD, SI::kPlain, nullptr, nullptr, x, x, in(sh->a_peers[r], lo_of(l, kPhAttn)), LLOut{},
+                   "sharded Wo");
         // gate|up rows of this rank -> every rank's gate|up
         if (!rc)
-            rc = strip(Ly.w_gate, 2 * (f1 - f0), D, SI::kRmsNorm, Ly.ffn_norm, nullptr,
-                       in(x_own, lo_of(l, kPhWo), nullptr, 0, 0),
-                       out(sh->gu_peers, f0, 2 * (f1 - f0), sh->gu_peers, F + f0, f1 - f0, lo_of(l, kPhGateUp)),
-                       "sharded gate|up");
-        // x[d0:d1] += Wdown silu(g) u -> every rank's x
+            rc = strip(Ly.w_gate, 2 * (f1 - f0), D, SI::kRmsNorm, Ly.ffn_norm, x, nullptr, nullptr, LLIn{},
+                       out(sh->gu_peers, f0, 2 * (f1 - f0), F + f0, f1 - f0, lo_of(l, kPhGateUp)), "sharded gate|up");
+        // x += Wdown silu(g) u, all rows (local)
         if (!rc)
-            rc = strip(Ly.w_down, d1 - d0, F, SI::kSiluMul, nullptr, nullptr,
-                       in(sh->gu_peers[r], lo_of(l, kPhGateUp), x_own, d0, lo_of(l, kPhWo)),
-                       out(sh->x_peers, d0, d1 - d0, nullptr, 0, 0, lo_of(l, kPhDown)), "sharded W_down");
+            rc = strip(Ly.w_down, D, F, SI::kSiluMul, nullptr, nullptr, x, x, in(sh->gu_peers[r], lo_of(l, kPhGateUp)),
+                       LLOut{}, "sharded W_down");
     }
     const int64_t NL = m->n_layer;
     if (!rc)
-        rc = strip(w_out, v1 - v0, D, SI::kRmsNorm, out_norm, nullptr, in(x_own, lo_of(NL - 1, kPhDown), nullptr, 0, 0),
-                   out(sh->logits_peers, v0, v1 - v0, nullptr, 0, 0, lo_of(NL, kPhLogits)), "sharded LM head");
+        rc = strip(w_out, v1 - v0, D, SI::kRmsNorm, out_norm, x, nullptr, nullptr, LLIn{},
+                   out(sh->logits_peers, v0, v1 - v0, 0, v1 - v0, lo_of(NL, kPhLogits)), "sharded LM head");
     if (!rc) {
         const int grid = static_cast<int>(std::min<int64_t>((V + 255) / 256, 148));
         ll_unpack_kernel<<<grid, 256, 0, s>>>(sh->logits_peers[r], logits, static_cast<int>(V), cnt,

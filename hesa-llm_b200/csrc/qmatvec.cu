@@ -998,22 +998,30 @@ cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k
 }
 
 cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, StripInput in, const float* norm_w,
-                            float eps, float scale, float* y, const LLIn& lin, const LLOut& lout,
-                            cudaStream_t stream) {
+                            float eps, float scale, const float* x, float* y, const float* resid, const LLIn& lin,
+                            const LLOut& lout, cudaStream_t stream) {
     StripPlan p;
-    if (!plan_strip(qtype, n_rows, k, p) || !lin.x || !lin.count || lout.world < 0 || lout.world > kPeerSyncMax ||
-        (lout.world > 0 && !lout.count) || (lout.world == 0 && (!y || lin.resid)))
+    const bool llx = lin.x != nullptr, tagged = lout.world > 0;
+    if (!plan_strip(qtype, n_rows, k, p) || (llx ? (!lin.count || x) : (!x || lin.resid)) || lout.world < 0 ||
+        lout.world > kPeerSyncMax || (tagged && (!lout.count || y || resid)) ||
+        (!tagged && (!y || lin.resid)) || (llx && tagged && resid))
         return cudaErrorInvalidValue;
     if (in == StripInput::kRmsNorm && (!norm_w || k > static_cast<int64_t>(kWarps) * kStripBatch * 256))
         return cudaErrorInvalidValue;
     const int xm = in == StripInput::kRmsNorm ? kXRmsNorm : in == StripInput::kSiluMul ? kXSiluMul : kXPlain;
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const int n = static_cast<int>(n_rows), kk = static_cast<int>(k);
-    if (lout.world > 0)
-        return launch_strip_qt<true, kOutTagged>(qtype, wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr,
+    if (llx && tagged)
+        return launch_strip_qt<true, kOutTagged>(qtype, wb, n, kk, nullptr, nullptr, scale, p, xm, norm_w, eps, nullptr,
                                                  PeerOut{}, lin, lout, stream);
-    return launch_strip_qt<true, kOutPlain>(qtype, wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, nullptr,
-                                            PeerOut{}, lin, lout, stream);
+    if (llx)
+        return launch_strip_qt<true, kOutPlain>(qtype, wb, n, kk, nullptr, y, scale, p, xm, norm_w, eps, resid,
+                                                PeerOut{}, lin, lout, stream);
+    if (tagged)
+        return launch_strip_qt<false, kOutTagged>(qtype, wb, n, kk, x, nullptr, scale, p, xm, norm_w, eps, nullptr,
+                                                  PeerOut{}, lin, lout, stream);
+    return launch_strip_qt<false, kOutPlain>(qtype, wb, n, kk, x, y, scale, p, xm, norm_w, eps, resid, PeerOut{}, lin,
+                                             lout, stream);
 }
 
 cudaError_t qmv_strip_gather_tagged(int qtype, const void* w, int64_t n_rows, int64_t k, const float* x, float scale,

@@ -65,12 +65,13 @@ cudaError_t qmv_strip_gather(int qtype, const void* w, int64_t n_rows, int64_t k
 namespace hesa_cuda {
 
 // The strip kernel of the sharded decode step: rows of y = scale * W . f(x)
-// (+ the residual) from tagged inputs (lin: x, and the residual when set) to
-// every rank as tagged words (lout), or, when lout.world is 0, to the plain
-// local y (no residual); f as qmv_strip_fused.
+// (+ a residual), f as qmv_strip_fused. Input: the tagged vector lin.x (and
+// a tagged residual lin.resid, tagged outputs only) when lin.x is set, else
+// the plain x. Output: every rank as tagged words (lout) when lout.world > 0,
+// else the plain local y (+ the plain resid when set).
 cudaError_t qmv_strip_shard(int qtype, const void* w, int64_t n_rows, int64_t k, StripInput in, const float* norm_w,
-                            float eps, float scale, float* y, const LLIn& lin, const LLOut& lout,
-                            cudaStream_t stream);
+                            float eps, float scale, const float* x, float* y, const float* resid, const LLIn& lin,
+                            const LLOut& lout, cudaStream_t stream);
 
 // Row-sharded matvec whose rows reach every rank as tagged words: row i to
 // element lout.off + i of lout.y[p] (of lout.y2[p] while the count is odd;

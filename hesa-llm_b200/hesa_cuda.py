@@ -87,13 +87,12 @@ SIGNATURES = [
 
 class Shard(ctypes.Structure):
     """hesa_cuda_shard (include/hesa_cuda.h): one rank of a head-sharded decode."""
-    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("x_peers", ctypes.c_void_p),
-                ("a_peers", ctypes.c_void_p), ("gu_peers", ctypes.c_void_p), ("logits_peers", ctypes.c_void_p),
-                ("token_count", ctypes.c_void_p)]
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("a_peers", ctypes.c_void_p),
+                ("gu_peers", ctypes.c_void_p), ("logits_peers", ctypes.c_void_p), ("token_count", ctypes.c_void_p)]
 
-    def __init__(self, rank, world, x, a, gu, logits, token_count):
-        super().__init__(rank, world, ctypes.cast(x, ctypes.c_void_p), ctypes.cast(a, ctypes.c_void_p),
-                         ctypes.cast(gu, ctypes.c_void_p), ctypes.cast(logits, ctypes.c_void_p), token_count)
+    def __init__(self, rank, world, a, gu, logits, token_count):
+        super().__init__(rank, world, ctypes.cast(a, ctypes.c_void_p), ctypes.cast(gu, ctypes.c_void_p),
+                         ctypes.cast(logits, ctypes.c_void_p), token_count)
 
 
 class HesaError(RuntimeError):

@@ -236,11 +236,13 @@ class ShardedDecoder:
     """One sequence decoded on `world` GPUs of a node (hesa_cuda_decode_step_sharded).
 
     Rank r keeps the Q, K, V rows of heads [r*H/world, (r+1)*H/world) (and of
-    its kv heads), their KV caches, and its balanced row share (row_range) of
-    Wo, gate|up, W_down and the LM head; the attention output, both residual
-    updates and gate|up are gathered into every rank by the kernels that make
-    them, as tagged 64-bit words that the consuming kernels wait for (peer
-    stores over NVLink, CUDA IPC mappings exchanged through `group`).
+    its kv heads), their KV caches, its balanced row share (row_range) of
+    gate|up and of the LM head, and all of Wo and W_down (every rank computes
+    their rows itself and keeps the residual locally); the attention output
+    and gate|up are gathered into every rank by the kernels that make them, as
+    tagged 64-bit words that the consuming kernels wait for (peer stores over
+    NVLink, CUDA IPC mappings exchanged through `group`). The logits equal
+    the unsharded step's bit for bit.
 
     full: the unsharded model on this rank's device, laid out as the decode
     step takes it -- a dict with "layers" (dicts of CUDA tensors: wq/wk/wv
@@ -249,7 +251,7 @@ class ShardedDecoder:
     fp16), "w_out", "out_norm" and "table" (the device rope table).
     """
 
-    FIELDS = ("x", "a", "gu", "logits", "count")
+    FIELDS = ("a", "gu", "logits", "count")
 
     def __init__(self, cfg: dict, full: dict, rank: int, world: int, group=None, device=None):
         import torch
@@ -262,10 +264,9 @@ class ShardedDecoder:
             raise ValueError(f"n_head {NH} and n_kv_head {NKV} must be multiples of world {world}")
         QD, KD = NH * HD, NKV * HD
         qd_r, kd_r = QD // world, KD // world
-        d0, d1 = row_range(D, rank, world)
         f0, f1 = row_range(F, rank, world)
         v0, v1 = row_range(V, rank, world)
-        self.rows = dict(d=(d0, d1), f=(f0, f1), v=(v0, v1))
+        self.rows = dict(f=(f0, f1), v=(v0, v1))
         self.layers = []
         for L in full["layers"]:
             qkv = torch.cat([L["wq"][rank * qd_r:(rank + 1) * qd_r], L["wk"][rank * kd_r:(rank + 1) * kd_r],
@@ -274,8 +275,8 @@ class ShardedDecoder:
             kc = L["k_cache"][:, rank * kd_r:(rank + 1) * kd_r].contiguous()
             vc = L["v_cache"][:, rank * kd_r:(rank + 1) * kd_r].contiguous()
             self.layers.append(dict(wq=qkv[:qd_r], wk=qkv[qd_r:qd_r + kd_r], wv=qkv[qd_r + kd_r:],
-                                    wo=L["wo"][d0:d1].contiguous(), w_gate=gu[:f1 - f0], w_up=gu[f1 - f0:],
-                                    w_down=L["w_down"][d0:d1].contiguous(), attn_norm=L["attn_norm"],
+                                    wo=L["wo"].contiguous(), w_gate=gu[:f1 - f0], w_up=gu[f1 - f0:],
+                                    w_down=L["w_down"].contiguous(), attn_norm=L["attn_norm"],
                                     ffn_norm=L["ffn_norm"], k_cache=kc, v_cache=vc, _keep=(qkv, gu)))
         self.w_out = full["w_out"][v0:v1].contiguous()
         self.out_norm, self.table = full["out_norm"], full["table"]
@@ -283,11 +284,11 @@ class ShardedDecoder:
                              cfg["qtype"])
         self.arr = H.make_layers(self.layers)
         self.ws = H.decode_workspace(self.model, device)
-        # one peer allocation per rank: tagged words (8 bytes) of x | a | gate,up
-        # | logits, then the token counter
-        # tagged vectors hold whole units of 256 words (the up half of gate|up
-        # starts at element F, a multiple of 256)
-        sizes = dict(x=8 * _align(D), a=8 * _align(QD), gu=16 * _align(F), logits=8 * _align(V), count=4)
+        # one peer allocation per rank: tagged words (8 bytes) of a | gate,up |
+        # logits, then the token counter; tagged vectors hold whole units of
+        # 256 words (the up half of gate|up starts at element F, a multiple of
+        # 256)
+        sizes = dict(a=8 * _align(QD), gu=16 * _align(F), logits=8 * _align(V), count=4)
         self.off, total = {}, 0
         for name in self.FIELDS:
             self.off[name] = total
@@ -299,7 +300,7 @@ class ShardedDecoder:
             dist.all_gather_object(handles, handle, group=group)
         self.base = [self.local if p == rank else H.peer_open(handles[p]) for p in range(world)]
         self.device = device
-        self.shard = H.Shard(rank, world, *[self._ptrs(n) for n in ("x", "a", "gu", "logits")],
+        self.shard = H.Shard(rank, world, *[self._ptrs(n) for n in ("a", "gu", "logits")],
                              self.local + self.off["count"])
         self.out = torch.empty(V, dtype=torch.float32, device=device)
 

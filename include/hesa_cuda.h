@@ -271,35 +271,37 @@ HESA_CUDA_API int hesa_cuda_decode_step(const hesa_cuda_model* model, const hesa
  * Rank r of `world` holds, per layer, the Q, K, V rows of its heads
  * [r*n_head/world, (r+1)*n_head/world) and kv heads likewise (joined: wk right
  * after wq's rows, wv after wk's), the KV caches of its kv heads
- * [ctx, n_kv_head/world * head_dim], and its balanced row share of Wo, of
- * gate|up (joined: its up rows right after its gate rows), of W_down and of
- * the LM head (rows [floor(r*n/world), floor((r+1)*n/world)) of each). Every
- * rank keeps the full residual vector. Per layer the attention output, the
- * Wo residual, gate|up and the W_down residual are gathered: the kernel that
- * produces each stores its part straight into every rank's buffer over
- * NVLink, every value as one 64-bit word with a tag naming the token and the
- * place in the step, and the kernel that consumes it reads each word once its
- * tag is the expected one (bounded wait: device status 4 when a peer does not
- * deliver in time) -- no fence, flag array or barrier launch per exchange.
- * The buffers are peer allocations (hesa_cuda_peer_alloc / _open) of 8 bytes
- * per element, each vector rounded up to whole units of 256 elements and
- * stored in the interleaved word order of hesa_cuda_qmatvec_gather_tagged
- * (16-byte aligned); arrays are host arrays of `world` device pointers,
- * entry p = rank p's buffer as mapped in this process. The decomposition of the
+ * [ctx, n_kv_head/world * head_dim], its balanced row share of gate|up
+ * (joined: its up rows right after its gate rows) and of the LM head (rows
+ * [floor(r*n/world), floor((r+1)*n/world)) of each), and ALL of Wo and
+ * W_down. Every rank keeps the residual vector itself. Per layer the
+ * attention output and gate|up are gathered: the kernel that produces each
+ * stores its part straight into every rank's buffer over NVLink, every value
+ * as one 64-bit word with a tag naming the token and the place in the step,
+ * and the kernel that consumes it reads each word once its tag is the
+ * expected one (bounded wait: device status 4 when a peer does not deliver in
+ * time) -- no fence, flag array or barrier launch per exchange. Wo and W_down
+ * run whole on every rank: two exchanges per layer instead of four. The
+ * buffers are peer allocations (hesa_cuda_peer_alloc / _open) of 8 bytes per
+ * element, each vector rounded up to whole units of 256 elements and stored
+ * in the interleaved word order of hesa_cuda_qmatvec_gather_tagged (16-byte
+ * aligned); arrays are host arrays of `world` device pointers, entry p =
+ * rank p's buffer as mapped in this process. The decomposition of the
  * reference's decode loop (docs/architecture.md:277-281) over the GPUs of one
  * node; no counterpart in the reference, which runs on one device. */
 typedef struct {
     int32_t rank, world;
-    uint64_t* const* x_peers;       /* [d_model] the residual vector */
     uint64_t* const* a_peers;       /* [n_head * head_dim] attention outputs */
     uint64_t* const* gu_peers;      /* [2 * d_ff] gate | up (up at element d_ff) */
     uint64_t* const* logits_peers;  /* [vocab] */
     uint32_t* token_count;          /* this rank's token counter (device uint32, zero-initialised) */
 } hesa_cuda_shard;
 
-/* One token of the decoder on this rank: `layers` hold this rank's shards,
- * w_out its LM-head rows; x_embed the token's embedding (the same on every
- * rank); logits [vocab] (this rank's device memory) receives all the logits.
+/* One token of the decoder on this rank: `layers` hold this rank's shards
+ * (wo and w_down the whole matrices), w_out its LM-head rows; x_embed the
+ * token's embedding (the same on every rank); logits [vocab] (this rank's
+ * device memory) receives all the logits, bit-identical to
+ * hesa_cuda_decode_step's.
  * Every rank must issue the same steps; the workspace is
  * hesa_cuda_decode_workspace_size(model) bytes (model = the full, unsharded
  * shape). n_head and n_kv_head must be multiples of world, n_layer < 512; the

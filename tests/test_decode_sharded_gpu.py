@@ -1,7 +1,8 @@
 """One sequence decoded on several GPUs (hesa_cuda_decode_step_sharded,
-sharding.ShardedDecoder): heads, their KV caches and row shares of Wo,
-gate|up, W_down and the LM head per rank; every kernel stores its rows into
-every rank as tagged 64-bit words and the next kernel waits per word (bounded).
+sharding.ShardedDecoder): heads, their KV caches and row shares of gate|up
+and the LM head per rank, Wo and W_down whole on every rank; the attention
+output and gate|up reach every rank as tagged 64-bit words stored by the
+kernels that make them, and the next kernel waits per word (bounded).
 
 World 1 (one GPU): the sharded step's logits are bit-identical to the
 unsharded decode step's and within rel-L2 1e-5 of the oracle, for
