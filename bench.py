@@ -687,6 +687,35 @@ def profile_batched(steps: int, batch: int):
     return 0
 
 
+def profile_sharded(steps: int):
+    """A 2-layer model of the 7B decode shapes: `steps` eager unsharded decode
+    steps, then `steps` of the sharded step on one rank (world 1), for an ncu
+    launch list that compares the two forms kernel by kernel."""
+    import torch
+    import hesa_cuda as H
+    import sharding
+    dev = torch.device("cuda", 0)
+    cfg = dict(DECODE_7B, n_layer=2)
+    d = build_decoder(cfg, dev, seed=77)
+    x = torch.empty(cfg["d_model"], device=dev)
+    pos = torch.tensor([DECODE_POS], dtype=torch.int32, device=dev)
+    tok = torch.tensor([1234], dtype=torch.int32, device=dev)
+    lg = torch.empty(cfg["vocab"], device=dev)
+    dec = sharding.ShardedDecoder(cfg, d, 0, 1, device=dev)
+    for _ in range(max(steps, 1)):
+        H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok, out=x)
+        H.decode_step(d["model"], d["arr"], d["out_norm"], d["w_out"], d["table"], x, pos, lg, d["ws"])
+    torch.cuda.synchronize()
+    for _ in range(max(steps, 1)):
+        H.embed(cfg["qtype"], d["emb"], cfg["d_model"], tok, out=x)
+        dec.step(x, pos)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(dec.logits(), lg))
+    dec.close()
+    log(f"profile sharded done: {steps} step(s) of each form, logits equal: {same}")
+    return 0
+
+
 def profile_shapes(steps: int):
     """A few eager launches of the shapes outside the sweep, for ncu: the
     Q4_0 4096 x 4096 matvec (batch 1, row-strip kernel) and the 70B down
@@ -1106,6 +1135,9 @@ def main():
     ap.add_argument("--profile-decode", action="store_true",
                     help="untimed: a 2-layer model of the 7B decode shapes, --steps eager decode steps "
                          "(for ncu launch lists of one step)")
+    ap.add_argument("--profile-sharded", action="store_true",
+                    help="untimed: a 2-layer model of the 7B decode shapes, --steps eager unsharded steps then "
+                         "--steps sharded steps on one rank (for an ncu launch list comparing the two)")
     ap.add_argument("--profile-shapes", action="store_true",
                     help="untimed: --steps eager launches each of Q4_0 4096x4096 and Q4_K 8192x28672 "
                          "(for ncu captures of the shapes outside the sweep)")
@@ -1121,6 +1153,8 @@ def main():
         return profile_decode(args.steps)
     if args.profile_shapes:
         return profile_shapes(args.steps)
+    if args.profile_sharded:
+        return profile_sharded(args.steps)
     if args.profile_batched:
         return profile_batched(args.steps, args.profile_batched)
     return run_gpu(args, rank, world, local_rank)
