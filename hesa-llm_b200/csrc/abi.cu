@@ -54,7 +54,10 @@ size_t hesa_cuda_row_bytes(int qtype, int64_t k) {
 size_t hesa_cuda_qmatvec_workspace_size(int qtype, int64_t n_out, int64_t k, int64_t batch) {
     if (!hesa_cuda::qtype_supported(qtype) || n_out <= 0 || k <= 0 || batch <= 0) return 0;
     size_t n = hesa_cuda::qmv_workspace_bytes(static_cast<int>(n_out));
-    if (batch >= 2 && k % 256 == 0) n = std::max(n, hesa_cuda::qmm_tc_workspace_bytes(qtype, n_out, k, batch));
+    if (batch >= 2 && k % 256 == 0) {
+        n = std::max(n, hesa_cuda::qmm_tc_workspace_bytes(qtype, n_out, k, batch));
+        n = std::max(n, hesa_cuda::qmm_blk_workspace_bytes(qtype, n_out, k, batch));
+    }
     return n;
 }
 
@@ -87,6 +90,13 @@ int hesa_cuda_qmatvec(int qtype, const void* w, int64_t n_out, int64_t k, const 
         if (!aligned16(workspace)) return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
         e = hesa_cuda::qmm_tc(qtype, w, n_out, k, x, ldx, batch, y, ldy, scale, workspace, s);
         if (e != cudaSuccess) return cuda_fail(e, "qmatvec tcgen05 kernel");
+    } else if (hesa_cuda::qmm_blk_eligible(qtype, w, n_out, k, batch) && (batch >= 3 || !strip_ok)) {
+        // Q8_0 / Q4_0 with several activation rows: tcgen05, one MMA per 32-weight block
+        const size_t need = hesa_cuda::qmm_blk_workspace_bytes(qtype, n_out, k, batch);
+        if (!workspace || workspace_bytes < need) return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace too small");
+        if (!aligned16(workspace)) return fail(HESA_CUDA_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+        e = hesa_cuda::qmm_blk(qtype, w, n_out, k, x, ldx, batch, y, ldy, scale, workspace, s);
+        if (e != cudaSuccess) return cuda_fail(e, "qmatvec tcgen05 block kernel");
     } else if (strip_ok) {
         // row strips: no workspace needed
         for (int64_t b = 0; b < batch; ++b) {

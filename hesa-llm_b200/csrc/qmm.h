@@ -17,4 +17,12 @@ size_t qmm_tc_workspace_bytes(int qtype, int64_t n_out, int64_t k, int64_t batch
 cudaError_t qmm_tc(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
                    float* y, int64_t ldy, float scale, void* workspace, cudaStream_t stream);
 
+// The same for Q8_0 / Q4_0 weights (qmm_tc_blk.cu): one tcgen05 MMA per 32-weight
+// block, the fp16 block scales applied in fp32 afterwards; one launch per 8
+// activation rows.
+bool qmm_blk_eligible(int qtype, const void* w, int64_t n_out, int64_t k, int64_t batch);
+size_t qmm_blk_workspace_bytes(int qtype, int64_t n_out, int64_t k, int64_t batch);
+cudaError_t qmm_blk(int qtype, const void* w, int64_t n_out, int64_t k, const float* x, int64_t ldx, int64_t batch,
+                    float* y, int64_t ldy, float scale, void* workspace, cudaStream_t stream);
+
 }  // namespace hesa_cuda

@@ -55,8 +55,11 @@ def test_batched_workspace_holds_staged_activations():
     assert one < b8 < b16
     assert b16 >= 43 * 12 * 1024
     assert H.workspace_bytes(12, 4096, 11008, 64) == b16      # 16 rows per launch pair
-    # types without the batched kernel keep the batch-1 size
-    assert H.workspace_bytes(8, 4096, 11008, 16) == H.workspace_bytes(8, 4096, 11008, 1)
+    # Q8_0 / Q4_0 keep slice partials for their tensor-core path too (8 rows per launch)
+    assert H.workspace_bytes(8, 4096, 11008, 16) > H.workspace_bytes(8, 4096, 11008, 1)
+    assert H.workspace_bytes(2, 4096, 4096, 3) > H.workspace_bytes(2, 4096, 4096, 1)
+    # a type without a batched kernel keeps the batch-1 size
+    assert H.workspace_bytes(14, 4096, 11008, 16) == H.workspace_bytes(14, 4096, 11008, 1)
 
 
 FAKE = 1 << 20  # non-null, 16-byte aligned, never dereferenced: validation fails first

@@ -1,5 +1,6 @@
-"""Batched matvec on the tensor cores (csrc/qmm_tc.cu, tcgen05) through the C ABI: Q4_K and
-Q5_K weights with 2..33 activation rows against the oracle (rel-L2 <= 1e-5
+"""Batched matvec on the tensor cores (csrc/qmm_tc.cu and, for Q8_0 / Q4_0,
+csrc/qmm_tc_blk.cu; tcgen05) through the C ABI: Q4_K, Q5_K, Q8_0 and Q4_0
+weights with 2..33 activation rows against the oracle (rel-L2 <= 1e-5
 per activation row), at the batched-decode shapes (4096 x 11008 and
 11008 x 4096, B in {2, 4, 8, 16}), ragged tiles, one-unit and 128-unit rows,
 strided x / y, non-finite activations, determinism, the workspace counters
@@ -76,6 +77,54 @@ def test_batched_edges(torch_cuda, name, n_out, k, batch):
     blocks = seeded(qt, n_out, k, 700 + n_out)
     x = O.gaussian((batch, k), 1.0, 800 + k)
     check_rows(run(torch_cuda, qt, blocks, x, scale=-0.5), O.qmatvec(qt, blocks, x, scale=-0.5))
+
+
+@pytest.mark.parametrize("name", ["Q8_0", "Q4_0"])
+@pytest.mark.parametrize("n_out,k", [(4096, 11008), (11008, 4096)])
+@pytest.mark.parametrize("batch", [3, 8, 16])
+def test_block_types_batched_decode_shapes(torch_cuda, name, n_out, k, batch):
+    """Q8_0 / Q4_0 on the tensor cores (qmm_tc_blk.cu): one MMA per 32-weight block."""
+    qt = O.QTYPES[name]
+    blocks = seeded(qt, n_out, k, 510 + qt + n_out)
+    x = O.gaussian((batch, k), 1.0, 610 + batch + k)
+    check_rows(run(torch_cuda, qt, blocks, x), O.qmatvec(qt, blocks, x))
+
+
+@pytest.mark.parametrize("name,n_out,k,batch", [
+    ("Q8_0", 100, 256, 3),       # one unit per row, ragged row tile
+    ("Q4_0", 4100, 768, 9),      # ragged last tile; three units (a one-unit copy); a second launch of one row
+    ("Q8_0", 64, 32768, 4),      # many K slices of one unit (rows too long for the strip kernel)
+    ("Q4_0", 64, 32768, 2),      # two rows on the tensor cores (the strip kernel does not take k > 24576)
+    ("Q8_0", 300, 1024, 20),     # launches of 8 + 8 + 4 rows
+])
+def test_block_types_batched_edges(torch_cuda, name, n_out, k, batch):
+    qt = O.QTYPES[name]
+    blocks = seeded(qt, n_out, k, 710 + n_out)
+    x = O.gaussian((batch, k), 1.0, 810 + k)
+    check_rows(run(torch_cuda, qt, blocks, x, scale=-0.5), O.qmatvec(qt, blocks, x, scale=-0.5))
+
+
+@pytest.mark.parametrize("name", ["Q8_0", "Q4_0"])
+def test_block_types_non_finite_row_determinism_and_counters(torch_cuda, name):
+    import hesa_cuda as H
+    torch = torch_cuda
+    qt, n, k, batch = O.QTYPES[name], 2048, 4096, 6
+    blocks = seeded(qt, n, k, 71)
+    x = O.gaussian((batch, k), 1.0, 72)
+    x[4, 1000] = np.nan
+    w = torch.from_numpy(blocks).cuda()
+    xt = torch.from_numpy(x).cuda()
+    ws = H.make_workspace(qt, n, k, batch)
+    y1 = H.qmatvec(qt, w, xt, workspace=ws).clone()
+    y2 = H.qmatvec(qt, w, xt, workspace=ws).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(y1[[0, 1, 2, 3, 5]], y2[[0, 1, 2, 3, 5]])
+    assert bool(torch.isnan(y1[4]).all())
+    keep = [0, 1, 2, 3, 5]
+    check_rows(y1.cpu().numpy()[keep], O.qmatvec(qt, blocks, x[keep]))
+    zero_bytes = (((n + 1) // 2) * 4 + 255) // 256 * 256
+    assert int(ws[:zero_bytes].count_nonzero()) == 0
+    assert H.device_status() == 0
 
 
 def test_batched_matches_single_rows(torch_cuda):
