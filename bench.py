@@ -421,23 +421,23 @@ BATCHED_SHAPES = ((4096, 11008), (11008, 4096))
 BATCHED_B = (1, 2, 4, 8, 16)
 
 
-def run_batched(dev, stream, reps: int = 20):
-    """Batched-decode matvec: Q4_K [n_out x k] against B activation rows, for
-    the two FFN shapes of the 7B model and B in BATCHED_B. Eight weight copies
-    (203 MB, more than L2) rotate inside one CUDA graph; device-timed.
+def run_batched(dev, stream, reps: int = 20, qname: str = "Q4_K", shapes=BATCHED_SHAPES, batches=BATCHED_B):
+    """Batched-decode matvec: `qname` [n_out x k] against B activation rows,
+    for the two FFN shapes of the 7B model and B in BATCHED_B. Eight weight
+    copies (more than L2) rotate inside one CUDA graph; device-timed.
     Returns {shape: {B: (us per matvec, algorithmic GB/s)}}, bytes = W + 4 B (k + n_out)."""
     import torch
     import hesa_cuda as H
-    qt, nw = QT["Q4_K"], 8
+    qt, nw = QT[qname], 8
     out = {}
     g = torch.Generator(device=dev)
     g.manual_seed(4321)
-    for (n, k) in BATCHED_SHAPES:
+    for (n, k) in shapes:
         w0 = H.quantize(qt, torch.randn((n, k), generator=g, device=dev) * 0.02)
         ws_list = [w0.clone() for _ in range(nw)]
         del w0
         res = {}
-        for B in BATCHED_B:
+        for B in batches:
             x = torch.randn((B, k), generator=g, device=dev)
             y = torch.empty((B, n), device=dev)
             wsp = H.make_workspace(qt, n, k, B, device=dev)
@@ -1015,6 +1015,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     # the 7B-shaped Q4_K decode step of one sequence (sharded over the ranks at N > 1)
     dec = run_decode(dev, stream, steps=max(args.steps, 20), warmup=args.warmup, pg=pg, rank=rank, world=world)
     batched = run_batched(dev, stream) if rank == 0 else None
+    # eight activation rows per block type (4096 x 11008): Q4_K / Q5_K scale-split
+    # kernel, Q8_0 / Q4_0 one MMA per 32-weight block, Q6_K one strip pass per row
+    batched_types = ({t: run_batched(dev, stream, qname=t, shapes=BATCHED_SHAPES[:1], batches=(8,))
+                      ["%dx%d" % BATCHED_SHAPES[0]][8] for t in ("Q4_0", "Q8_0", "Q4_K", "Q5_K", "Q6_K")}
+                     if rank == 0 else None)
     p70_ms, p70_local_ms = run_proj70b(dev, stream, rank, world, pg=pg)
 
     # max over ranks
@@ -1092,6 +1097,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
             "batched": {"workload": "Q4_K [n_out x k] times B activation rows (batched decode), "
                                     "one launch per 16 rows on the tensor cores (B >= 3; B = 2 as two batch-1 passes)",
                         "us_and_gbs": batched,
+                        "b8_by_type_4096x11008": batched_types,
+                        "b8_by_type_paths": "Q4_K/Q5_K: tcgen05, scale folded into two weight operands; Q8_0/Q4_0: "
+                                            "tcgen05, one MMA per 32-weight block; Q6_K: eight batch-1 strip passes",
                         "timing": "8 rotating weight copies (203 MB > L2) in one CUDA graph, CUDA events, rank 0"},
             "proj70b": {"workload": "70B-shaped Q4_K projections, batch 1: Wq, Wo 8192x8192; Wk, Wv 1024x8192; "
                                    "gate, up 28672x8192; down 8192x28672 ([n_out x k])",

@@ -78,10 +78,11 @@ HESA_CUDA_API size_t hesa_cuda_qmatvec_workspace_size(int qtype, int64_t n_out, 
  * TensorView b, TensorView out, float scale) (include/hesa/backend.hpp:43-44)
  * whose CPU semantics are cpu_matmul_f32 (src/backend/cpu_backend.cpp:24-41):
  * a = W [n_out, k], b = x^T [k, batch], out = y^T [n_out, batch].
- * Batch 1 is one streaming pass over W on CUDA cores. Q4_K and Q5_K with
- * batch >= 3 (k a multiple of 256; batch 2 too when k > 24576) run on the
- * tensor cores, reading W once per 16 activation rows; the other types, and
- * batch 2 with k <= 24576, make one pass per batch column.
+ * Batch 1 is one streaming pass over W on CUDA cores. Q4_K, Q5_K, Q8_0 and
+ * Q4_0 with batch >= 3 (k a multiple of 256; batch 2 too when k > 24576) run
+ * on the tensor cores, reading W once per 16 activation rows (Q4_K, Q5_K) or
+ * once per 8 (Q8_0, Q4_0); Q6_K, and batch 2 with k <= 24576, make one pass
+ * per batch column.
  * x and y must be 16-byte aligned with ldx, ldy multiples of 4.
  * The workspace is used by the batched kernel and the split-row kernel (rows
  * longer than 24576 weights, or matrices too tall for one strip of rows per
