@@ -667,21 +667,22 @@ def profile_decode(steps: int):
     return 0
 
 
-def profile_batched(steps: int, batch: int):
-    """A few eager batched matvecs (Q4_K 4096 x 11008, `batch` activation rows)
-    on one weight copy, small enough for an ncu capture of one launch."""
+def profile_batched(steps: int, batch: int, qname: str = "Q4_K"):
+    """A few eager batched matvecs (`qname` 4096 x 11008, `batch` activation
+    rows) on one weight copy, small enough for an ncu capture of one launch."""
     import torch
     import hesa_cuda as H
     dev = torch.device("cuda", 0)
     n, k = BATCHED_SHAPES[0]
     g = torch.Generator(device=dev)
     g.manual_seed(11)
-    w = H.quantize(QT["Q4_K"], torch.randn((n, k), generator=g, device=dev) * 0.02)
+    qt = QT[qname]
+    w = H.quantize(qt, torch.randn((n, k), generator=g, device=dev) * 0.02)
     x = torch.randn((batch, k), generator=g, device=dev)
     y = torch.empty((batch, n), device=dev)
-    ws = H.make_workspace(QT["Q4_K"], n, k, batch, device=dev)
+    ws = H.make_workspace(qt, n, k, batch, device=dev)
     for _ in range(max(steps, 1)):
-        H.qmatvec(QT["Q4_K"], w, x, y=y, workspace=ws)
+        H.qmatvec(qt, w, x, y=y, workspace=ws)
     torch.cuda.synchronize()
     log(f"profile batched done: {steps} launch(es) of B={batch}, outputs finite: {bool(torch.isfinite(y).all())}")
     return 0
@@ -1140,6 +1141,8 @@ def main():
                     help="untimed: build inputs, run --steps plain steps, exit (for ncu captures)")
     ap.add_argument("--profile-batched", type=int, default=0, metavar="B",
                     help="run --steps eager batched matvecs with B activation rows (for an ncu capture) and exit")
+    ap.add_argument("--profile-type", default="Q4_K", choices=sorted(QT),
+                    help="block type of the --profile-batched matrix")
     ap.add_argument("--profile-decode", action="store_true",
                     help="untimed: a 2-layer model of the 7B decode shapes, --steps eager decode steps "
                          "(for ncu launch lists of one step)")
@@ -1164,7 +1167,7 @@ def main():
     if args.profile_sharded:
         return profile_sharded(args.steps)
     if args.profile_batched:
-        return profile_batched(args.steps, args.profile_batched)
+        return profile_batched(args.steps, args.profile_batched, args.profile_type)
     return run_gpu(args, rank, world, local_rank)
 
 
