@@ -245,6 +245,11 @@ qmm_tc_kernel(const __grid_constant__ CUtensorMap wmap2, const __grid_constant__
                                 (u0 + 2 * g) * UB / 2, rt * kRows, &wfull[slot]);
                 }
             }
+            // every copy of this CTA is issued: the next kernel on the stream may
+            // start its CTAs on the SMs this grid leaves (its weight copies overlap
+            // this grid's tail; it reads x and writes y only after this grid ends).
+            // Measured: B = 8 on 4096 x 11008, 24.2 -> 21.9 us per matvec
+            grid_dep_launch();
             // the last copies into each slot have landed before the CTA may exit
             for (int c = cq > kWSlots ? cq - kWSlots : 0; c < cq; ++c)
                 if (!mbar_wait_bounded(&wfull[c % kWSlots], static_cast<uint32_t>(c / kWSlots) & 1u, status,
