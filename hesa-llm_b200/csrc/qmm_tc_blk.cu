@@ -18,11 +18,12 @@
 //     mbarrier;
 //   * epilogue warps (two per lane quarter, one per half of the activation
 //     rows) read the accumulators back (tcgen05.ld) and scale them.
-// The A operand and the accumulators are double-buffered (2 x 8 x 32 = 512
-// TMEM columns), so the transform of unit q+1, the MMAs of unit q and the
-// epilogue of unit q-1 overlap. Work split, weight streaming (2-D TMA tensor
-// copies of 128 rows, no multicast) and the ticketed, ordered sum of K slices
-// are those of qmm_tc.cu.
+// The A operand (two 32 KB buffers in shared memory) and the accumulators (two
+// sets of 8 x 32 TMEM columns: all 512) are double-buffered, so the transform
+// of unit q+1, the MMAs of unit q and the epilogue of unit q-1 overlap. Work
+// split, weight streaming (2-D TMA tensor copies of 128 rows, no multicast),
+// the ticketed, ordered sum of K slices and the dependent-launch trigger after
+// a CTA's last weight copy are those of qmm_tc.cu.
 #include "hesa_common.cuh"
 #include "qtypes.cuh"
 #include "xdigits.cuh"
