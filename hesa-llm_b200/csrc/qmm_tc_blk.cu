@@ -10,10 +10,11 @@
 //   Q8_0: y_b += d_j * s_b * (65536*D2 + 256*D1 + D0)      (q signed, A = s8)
 //   Q4_0: y_b += d_j * (s_b * (...) - 8 * sum_{k in j} x_bk) (q = 0..15, A = u8)
 // Per unit of 256 weights (8 blocks) of a 128-row tile:
-//   * transform warps (two per TMEM lane quarter, one per half unit) copy
-//     their row's levels out of the TMA-staged GGUF blocks into the A operand
-//     in shared memory (canonical K-major core matrices, one byte per level)
-//     and the eight block scales into a small header ring;
+//   * transform warps (16 rows of the tile each, lanes over (row, block)
+//     pieces so that their shared-memory reads meet no bank conflict) copy the
+//     levels out of the TMA-staged GGUF blocks into the A operand in shared
+//     memory (canonical K-major core matrices, one byte per level) and the
+//     eight block scales of every row into a small header ring;
 //   * one thread of the MMA warp issues the eight MMAs and commits them to an
 //     mbarrier;
 //   * epilogue warps (two per lane quarter, one per half of the activation
@@ -70,7 +71,6 @@ constexpr uint32_t kAB = kRows * 256;
 // epilogue warp's 12 columns (rows 4h .. 4h+3, all planes) are contiguous
 __host__ __device__ constexpr int tc_cp(int p, int b) { return (b >> 2) * 16 + p * 4 + (b & 3); }
 
-__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
 // Wait for phase `parity` of `bar` by polling, without suspending the thread:
 // for the MMA thread, which hands every unit on and whose wake-up from a
 // suspending wait (measured ~0.3 us) would be on the critical path. Bounded like
@@ -174,80 +174,72 @@ __device__ __forceinline__ void tc_store_pair(const float (&v)[8], int b, int la
     if (lane == 0) info[0] = s;
 }
 
-// The levels of blocks 4hf .. 4hf+3 of one unit of one row (the 4 x BB bytes
-// at `p`, 8-byte aligned) into the A operand row `arow`, and their four fp16
-// scales (two per word, block order) into d01 / d23.
+// One transform warp's share of a unit: rows 16w .. 16w+15 of the tile, all 8
+// blocks, from the staged GGUF copy (row r's unit at `copy + r * row_stride +
+// unit_off`) into the A operand `abuf` (block j of row r: 32 levels at
+// k-step j, two 16-byte k halves) and the rows' fp16 block scales into
+// `hdr` (row r: 8 scales in block order).
+//
+// Lanes take (row, block) pieces, not whole rows: the rows of a copy are 272
+// (Q8_0) or 288 (Q4_0) bytes apart, so 32 lanes on 32 rows read four banks
+// between them. Q8_0: a step is 8 rows x 4 blocks of one parity (blocks
+// 0,2,4,6 start 0/17/2/19 words mod 32 into a row, rows 4 banks apart: all 32
+// lanes on distinct banks), and each quarter-warp writes 8 rows of one block,
+// 128 contiguous bytes of A. Q4_0: a step is 4 rows x 8 blocks (rows 8 banks
+// apart, blocks 0,4,9,13,18,22,27,31 words in: distinct banks).
 template <int QT>
-__device__ __forceinline__ void blk_unpack_half(const uint8_t* p, uint8_t* arow, int hf, uint32_t& d01,
-                                                uint32_t& d23) {
+__device__ __forceinline__ void blk_transform(const uint8_t* copy, int row_stride, int unit_off, uint8_t* abuf,
+                                              uint4* hdr, int warp, int lane) {
     constexpr uint32_t AHALF = (kRows / 8) * 128, ASTEP = 2 * AHALF;
+    auto put = [&](int r, int j, uint32_t d, const uint32_t (&lo)[4], const uint32_t (&hi)[4]) {
+        uint8_t* dst = abuf + j * ASTEP + (r >> 3) * 128 + (r & 7) * 16;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(dst + AHALF) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        reinterpret_cast<unsigned short*>(hdr + r)[j] = static_cast<unsigned short>(d);
+    };
     if constexpr (QT == kQ8_0) {
-        // four 34-byte blocks = 136 bytes: 34 words
-        uint32_t w[34];
 #pragma unroll
-        for (int i = 0; i < 17; ++i) {
-            const uint2 v = lds64(p + 8 * i);
-            w[2 * i] = v.x;
-            w[2 * i + 1] = v.y;
-        }
-        uint32_t d[4];
+        for (int g = 0; g < 2; ++g) {
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-            // block jj starts at byte 34 jj: even blocks on a word boundary (d in
-            // the low half, levels from byte 2 on), odd blocks two bytes in (d in
-            // the high half of the word before, levels word-aligned)
-            uint32_t q[8];
-            if ((jj & 1) == 0) {
-                const int e = (34 * jj) / 4;
-                d[jj] = w[e] & 0xFFFFu;
+            for (int par = 0; par < 2; ++par) {
+                const int r = 16 * warp + 8 * g + (lane & 7);
+                const int j = 2 * (lane >> 3) + par;
+                // block j (34 bytes: d, then 32 levels) starts 34j bytes into the
+                // unit: on a word boundary for even j, two bytes past one for odd j
+                const uint8_t* b = copy + static_cast<size_t>(r) * row_stride + unit_off + 34 * j - 2 * par;
+                uint32_t w[9];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) q[c] = prmt(w[e + c], w[e + c + 1], 0x5432u);
-            } else {
-                const int e = (34 * jj - 2) / 4;
-                d[jj] = w[e] >> 16;
+                for (int c = 0; c < 9; ++c) w[c] = *reinterpret_cast<const uint32_t*>(b + 4 * c);
+                uint32_t q[8];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) q[c] = w[e + 1 + c];
+                for (int c = 0; c < 8; ++c) q[c] = par ? w[c + 1] : prmt(w[c], w[c + 1], 0x5432u);
+                const uint32_t lo[4] = {q[0], q[1], q[2], q[3]}, hi[4] = {q[4], q[5], q[6], q[7]};
+                put(r, j, par ? (w[0] >> 16) : (w[0] & 0xFFFFu), lo, hi);
             }
-            const int j = 4 * hf + jj;   // block = k-step
-            *reinterpret_cast<uint4*>(arow + j * ASTEP) = make_uint4(q[0], q[1], q[2], q[3]);
-            *reinterpret_cast<uint4*>(arow + j * ASTEP + AHALF) = make_uint4(q[4], q[5], q[6], q[7]);
         }
-        d01 = d[0] | (d[1] << 16);
-        d23 = d[2] | (d[3] << 16);
     } else {
-        // four 18-byte blocks = 72 bytes: 18 words
-        uint32_t w[18];
 #pragma unroll
-        for (int i = 0; i < 9; ++i) {
-            const uint2 v = lds64(p + 8 * i);
-            w[2 * i] = v.x;
-            w[2 * i + 1] = v.y;
-        }
-        uint32_t d[4];
+        for (int st = 0; st < 4; ++st) {
+            const int r = 16 * warp + 4 * st + (lane & 3);
+            const int j = lane >> 2;
+            // block j (18 bytes: d, then 16 bytes of nibbles) starts 18j bytes in:
+            // on a word boundary for even j, two bytes past one for odd j
+            const int sh = (18 * j) & 2;
+            const uint8_t* b = copy + static_cast<size_t>(r) * row_stride + unit_off + 18 * j - sh;
+            uint32_t w[5];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-            uint32_t q[4];
-            if ((jj & 1) == 0) {
-                const int e = (18 * jj) / 4;
-                d[jj] = w[e] & 0xFFFFu;
+            for (int c = 0; c < 5; ++c) w[c] = *reinterpret_cast<const uint32_t*>(b + 4 * c);
+            const uint32_t sel = sh ? 0x7654u : 0x5432u;
+            uint32_t lo[4], hi[4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) q[c] = prmt(w[e + c], w[e + c + 1], 0x5432u);
-            } else {
-                const int e = (18 * jj - 2) / 4;
-                d[jj] = w[e] >> 16;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) q[c] = w[e + 1 + c];
+            for (int c = 0; c < 4; ++c) {
+                // byte i: level of weight i in the low nibble, of weight i + 16 in the high one
+                const uint32_t qv = prmt(w[c], w[c + 1], sel);
+                lo[c] = qv & 0x0F0F0F0Fu;
+                hi[c] = (qv >> 4) & 0x0F0F0F0Fu;
             }
-            // byte i: level of weight i in the low nibble, of weight i + 16 in the high one
-            const int j = 4 * hf + jj;
-            *reinterpret_cast<uint4*>(arow + j * ASTEP) =
-                make_uint4(q[0] & 0x0F0F0F0Fu, q[1] & 0x0F0F0F0Fu, q[2] & 0x0F0F0F0Fu, q[3] & 0x0F0F0F0Fu);
-            *reinterpret_cast<uint4*>(arow + j * ASTEP + AHALF) =
-                make_uint4((q[0] >> 4) & 0x0F0F0F0Fu, (q[1] >> 4) & 0x0F0F0F0Fu, (q[2] >> 4) & 0x0F0F0F0Fu,
-                           (q[3] >> 4) & 0x0F0F0F0Fu);
+            put(r, j, (w[0] >> (8 * sh)) & 0xFFFFu, lo, hi);
         }
-        d01 = d[0] | (d[1] << 16);
-        d23 = d[2] | (d[3] << 16);
     }
 }
 
@@ -441,7 +433,7 @@ qmm_blk_kernel(const __grid_constant__ CUtensorMap wmapN, const __grid_constant_
             cur_s = s;
         }
         if (is_x) {
-            // ---- transform: unit ui of this thread's row, blocks 4hf .. 4hf+3, into A buffer q%2 ----
+            // ---- transform: unit ui of this warp's 16 rows into A buffer q%2 ----
             for (int ui = 0; ui < nu; ++ui, ++q) {
                 const int cqu = cq_base + ui / SU, slot = cqu % kWSlots;
                 const int wd = SU * (ui / SU) + SU <= nu ? SU : 1;
@@ -459,13 +451,9 @@ qmm_blk_kernel(const __grid_constant__ CUtensorMap wmapN, const __grid_constant_
                 }
                 ok = __all_sync(0xffffffffu, ok);
                 if (ok) {
-                    // a copy of wd units is [row][wd units]; this unit's half at 4 blocks per half
-                    const uint8_t* p = sw + static_cast<size_t>(slot) * SLOT + static_cast<size_t>(row_t) * (wd * UB) +
-                                       (ui % SU) * UB + hf * (UB / 2);
-                    uint8_t* arow = sa + static_cast<size_t>(kAB) * (q & 1) + (row_t >> 3) * 128 + (row_t & 7) * 16;
-                    uint32_t d01, d23;
-                    blk_unpack_half<QT>(p, arow, hf, d01, d23);
-                    reinterpret_cast<uint2*>(&hdrs[q % kHdrRing][row_t])[hf] = make_uint2(d01, d23);
+                    // a copy of wd units is [row][wd units]
+                    blk_transform<QT>(sw + static_cast<size_t>(slot) * SLOT, wd * UB, (ui % SU) * UB,
+                                      sa + static_cast<size_t>(kAB) * (q & 1), hdrs[q % kHdrRing], warp, lane);
                 }
                 fence_proxy_async_smem();   // the tensor cores read the operand through the async proxy
                 __syncwarp();
