@@ -62,6 +62,19 @@ def test_batched_workspace_holds_staged_activations():
     assert H.workspace_bytes(14, 4096, 11008, 16) == H.workspace_bytes(14, 4096, 11008, 1)
 
 
+@pytest.mark.parametrize("qt", [2, 8])
+def test_block_type_batched_workspace(qt):
+    # Q8_0 / Q4_0 take the tensor-core path only for k a multiple of 256: other
+    # widths keep the batch-1 size; one plan serves every launch of 8 rows
+    one = H.workspace_bytes(qt, 4096, 4096, 1)
+    assert H.workspace_bytes(qt, 4096, 4096 + 32, 8) == H.workspace_bytes(qt, 4096, 4096 + 32, 1)
+    b3, b8, b64 = (H.workspace_bytes(qt, 4096, 4096, b) for b in (3, 8, 64))
+    assert one < b3 == b8 == b64
+    # tickets (one int per two rows, 256-byte aligned) plus at least two slices of
+    # 8-row partial sums
+    assert b8 >= ((4096 + 1) // 2) * 4 + 2 * 4096 * 8 * 4
+
+
 FAKE = 1 << 20  # non-null, 16-byte aligned, never dereferenced: validation fails first
 
 
